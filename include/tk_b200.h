@@ -1,0 +1,149 @@
+/*
+ * tk_b200.h — C ABI of the B200 (sm_100a) implementation of the
+ * ThunderKittens-SM7x hot path.
+ *
+ * Plain C: pointers, sizes, a CUDA stream and a cudaError_t result. Binary16
+ * (FP16) buffers are passed as `const void*` holding IEEE binary16 elements.
+ * Reference citations are relative to the ThunderKittens-SM7x project root.
+ *
+ * Common contract (from include/tk_sm7x/gemm.cuh:8-14 and attention.cuh:8-14):
+ *   - All pointers are device-accessible on the current device. The caller owns
+ *     every buffer and keeps it alive until the stream work completes.
+ *   - Work is enqueued asynchronously on `stream` (0 = legacy default stream;
+ *     any stream, including non-blocking ones, is accepted).
+ *   - Invalid arguments return cudaErrorInvalidValue before anything is
+ *     enqueued: outputs are untouched and the thread's pending CUDA error is left
+ *     as it was (src/gemm.cu:190-195, src/attention.cu:66-68).
+ *   - A valid call first clears the pending error, enqueues, and returns
+ *     cudaGetLastError() (src/gemm.cu:197-205). Success covers validation and
+ *     launch only; execution errors surface at synchronisation.
+ *   - A device without compute capability 10.0 returns
+ *     cudaErrorInvalidDeviceFunction (the library holds sm_100a code only).
+ */
+#ifndef TK_B200_H
+#define TK_B200_H
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- GEMM ------------------------------------------------------------------ */
+
+/* Replaces tk_sm7x::gemm_f16_f16_f32_nn (include/tk_sm7x/gemm.cuh:15-20,
+ * src/gemm.cu:184-206). C[m x n] = A[m x k] * B[k x n]; A, B row-major binary16,
+ * C row-major FP32 with FP32 accumulation. m, n, k positive multiples of 16;
+ * lda >= k, ldb >= n, ldc >= n; A, B, C must not overlap. Only the logical
+ * m x n cells of C are written: columns n..ldc-1 of each row are untouched.
+ * Any element alignment of the pointers and any leading dimension satisfying
+ * the rule above is accepted (16-byte aligned rows take the TMA path directly;
+ * other operands are first copied into stream-ordered scratch buffers). */
+TK_API cudaError_t tk_gemm_f16_f16_f32_nn(int m, int n, int k, const void* a, int lda,
+                                          const void* b, int ldb, float* c, int ldc,
+                                          cudaStream_t stream);
+
+/* GEMM with a fused row-statistics epilogue: in addition to C, row_max[i] and
+ * row_sum[i] receive the maximum and sum of row i of the FP32 result C. The
+ * reduction order is fixed: each 16-column group is reduced by the canonical
+ * balanced tree (tests/row_reduce_reference.cuh:16-24), then groups combine
+ * pairwise level by level in column order, an odd last partial carried up.
+ * Max ties pick the right operand (include/tk_sm7x/row_reduce_ops.cuh:11-15).
+ * Generalises examples/gemm_row_stats.cu:17-40 from one 16x16 tile to full rows.
+ * row_max and row_sum hold m floats each and must not overlap C or each other.
+ * The per-tile partials (m * ceil(n / 256) float pairs) live in a scratch
+ * buffer taken from the stream-ordered allocator (cudaMallocAsync) and returned
+ * with cudaFreeAsync on the same stream. */
+TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const void* a,
+                                                   int lda, const void* b, int ldb,
+                                                   float* c, int ldc, float* row_max,
+                                                   float* row_sum, cudaStream_t stream);
+
+/* Tuning knob, no counterpart in the reference (whose tile choice is the fixed
+ * rule of src/gemm.cu:50-57): 0 = choose by problem size (default), 1 = one CTA
+ * per 128 x 256 tile, 2 = CTA pairs on 256 x 256 tiles. Process-wide; returns
+ * the previous setting. */
+TK_API int tk_gemm_set_cta_group(int cta_group);
+
+/* ---- tile row operations --------------------------------------------------- */
+/* `tiles` holds n_tiles contiguous 16x16 row-major FP32 tiles (256 floats,
+ * 1 KiB each). Reductions write 16 floats per tile (row order); softmax writes
+ * 256 floats per tile. n_tiles == 0 is a valid empty call (nothing enqueued).
+ * tiles and out must be 4-byte aligned; softmax outputs may alias the input
+ * exactly (in place) but must not partially overlap it. */
+
+/* Per-row sum, balanced column-order tree, replaces tk_sm7x::row_sum
+ * (include/tk_sm7x/reduce.cuh:43-46) for a batch of tiles. */
+TK_API cudaError_t tk_tile_row_sum_f32(const float* tiles, size_t n_tiles, float* out,
+                                       cudaStream_t stream);
+/* Per-row max, same tree, ties pick the right operand; replaces tk_sm7x::row_max
+ * (include/tk_sm7x/reduce.cuh:48-51). */
+TK_API cudaError_t tk_tile_row_max_f32(const float* tiles, size_t n_tiles, float* out,
+                                       cudaStream_t stream);
+/* exp(x - row_max) / row_sum with the same trees; replaces
+ * tk_sm7x::row_softmax (include/tk_sm7x/softmax.cuh:54-64). */
+TK_API cudaError_t tk_tile_row_softmax_f32(const float* tiles, size_t n_tiles,
+                                           float* out, cudaStream_t stream);
+/* Row i uses columns 0..i; the rest are exactly 0. Replaces
+ * tk_sm7x::row_softmax_causal (include/tk_sm7x/softmax.cuh:69-81). */
+TK_API cudaError_t tk_tile_row_softmax_causal_f32(const float* tiles, size_t n_tiles,
+                                                  float* out, cudaStream_t stream);
+/* All four from one read of the input. Any output may be NULL (skipped) but not
+ * all of them; outputs must not overlap each other or the input. */
+TK_API cudaError_t tk_tile_row_ops_f32(const float* tiles, size_t n_tiles,
+                                       float* row_sum, float* row_max, float* softmax,
+                                       float* softmax_causal, cudaStream_t stream);
+
+/* ---- attention forward ------------------------------------------------------ */
+
+/* Replace tk_sm7x::attention_forward_16x16[_causal] (include/tk_sm7x/
+ * attention.cuh:15-23, src/attention.cu:76-86): softmax(Q K^T / 4) V for one
+ * contiguous row-major 16x16 binary16 tile each of Q, K, V; the normalised
+ * probabilities are rounded to binary16 (nearest even) before the PV product;
+ * out is a contiguous row-major 16x16 FP32 tile. Q, K, V may alias each other
+ * but not out. Inputs must be finite. */
+TK_API cudaError_t tk_attention_forward_16x16(const void* q, const void* k,
+                                              const void* v, float* out,
+                                              cudaStream_t stream);
+TK_API cudaError_t tk_attention_forward_16x16_causal(const void* q, const void* k,
+                                                     const void* v, float* out,
+                                                     cudaStream_t stream);
+
+/* General forward over [batch, heads, seq, head_dim] contiguous binary16 Q, K, V
+ * and FP32 out of the same shape: out = softmax(Q K^T * scale [causal: key t <=
+ * query row]) V with the probabilities rounded to binary16 before the PV product.
+ * head_dim in {16, 32, 64, 128}; seq >= 1 (tails allowed); batch, heads >= 1.
+ * When seq <= 128 the probabilities are normalised before rounding (the exact
+ * semantics of the 16x16 entry points); for longer sequences the kernel keeps a
+ * running max and rounds exp(s - running_max) before the PV product, then
+ * divides by the running sum (online softmax), which stays inside the
+ * generalised error bound. Q, K, V may alias each other but not out. */
+TK_API cudaError_t tk_attention_forward_f16(const void* q, const void* k, const void* v,
+                                            float* out, int batch, int heads, int seq,
+                                            int head_dim, float scale, int causal,
+                                            cudaStream_t stream);
+
+/* ---- status ------------------------------------------------------------------ */
+
+/* Every wait inside the library's kernels is bounded. A kernel that gives up on
+ * a wait records a nonzero code in a per-device status word and returns
+ * instead of hanging. This reads (and with clear != 0 resets) that word for the
+ * current device; it synchronises the device. */
+TK_API cudaError_t tk_device_status(uint32_t* status, int clear);
+
+/* Version of this C ABI (major * 100 + minor). */
+TK_API int tk_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TK_B200_H */

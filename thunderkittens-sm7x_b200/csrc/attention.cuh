@@ -1,0 +1,502 @@
+// attention.cuh — attention forward, softmax(Q K^T * scale) V, on sm_100a.
+//
+// Generalises the one-tile kernel of ThunderKittens-SM7x (src/attention.cu:10-60,
+// one 16 x 16 tile, scale 1/4, one warp) to [batch, heads, seq, head_dim].
+// Probabilities are rounded to binary16 (nearest even) before the PV product,
+// as in src/attention.cu:43-47.
+//
+// Layout in HBM: Q, K, V are [B*H, S, D] binary16, out is [B*H, S, D] FP32.
+// Each CTA owns one (batch, head) and two consecutive 128-row query tiles; it
+// streams 128-key blocks of K and V through a four-slot shared-memory ring
+// (TMA, 128-byte swizzle, D padded to a multiple of 64 with TMA zero fill).
+//
+// Tensor memory (512 columns): tile g uses S_g = cols [256g, 256g + 128) for the
+// FP32 scores and O_g = cols [256g + 128, 256g + 256) for the FP32 output
+// accumulator. Its softmax warpgroup reads S_g, writes the binary16
+// probabilities back over the first 64 columns of S_g, and the MMA warp
+// consumes them directly from TMEM (tcgen05.mma with A in tensor memory).
+//
+// MMA issue order per key block j:  S0_j, PV1_{j-1}, S1_j, PV0_j.
+// While the tensor core runs PV1_{j-1} and S1_j, warpgroup 0 does the softmax
+// of S0_j, and vice versa, so exponentials overlap matrix products. Because
+// tcgen05 operations of one thread complete in order, the commit that
+// announces S_g,j also guarantees PV_g,j-1 has finished: the softmax warpgroup
+// may then rescale O_g in place.
+//
+// Rounding semantics: when the whole sequence fits one key block (S <= 128)
+// the row max and sum are final before rounding, so P = rn16(exp(s - m) / l)
+// exactly as the reference. For longer sequences the kernel keeps a running
+// max m and rounds exp(s - m) (online softmax), divides by the running sum at
+// the end, and stays inside the generalised bound
+// (512*2^-23 + 2^-11 + gamma(2S)) * sum_t |V[t, c]|.
+#pragma once
+
+#include <climits>
+
+#include "tk_host.cuh"
+#include "tk_ptx.cuh"
+
+namespace tk {
+namespace attn {
+
+constexpr int kThreads = 320;  // warps 0-7: two softmax warpgroups, 8: TMA, 9: MMA
+constexpr int kBlockQ = 128;
+constexpr int kBlockKV = 128;
+constexpr int kKvSlots = 4;
+constexpr uint32_t kTmemCols = 512;
+
+template <int kDPad>
+struct Cfg {
+    static constexpr int kTileBytes = kBlockQ * kDPad * 2;   // one Q / K / V tile
+    static constexpr int kBoxes = kDPad / 64;                 // 64-column TMA boxes per tile
+    static constexpr int kQOffset = 0;                        // Q0, Q1
+    static constexpr int kKvOffset = 2 * kTileBytes;          // KV ring
+    static constexpr int kBarOffset = kKvOffset + kKvSlots * kTileBytes;
+    static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
+    static constexpr uint32_t kIdescS = idesc_f16_f32(128, kBlockKV, 0, 0);
+    static constexpr uint32_t kIdescO = idesc_f16_f32(128, kDPad, 0, 1);
+};
+
+struct Params {
+    int seq;           // S
+    int head_dim;      // D (valid output columns)
+    int pairs;         // ceil(S / 256): query-tile pairs per (batch, head)
+    int bh;            // B * H
+    float scale_log2;  // scale * log2(e)
+    int causal;
+    float* out;
+    bool out_vec4;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int kDPad>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, const Params p) {
+    using C = Cfg<kDPad>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_base);
+    const uint32_t bars = base + C::kBarOffset;
+    auto kv_full = [&](int s) { return bars + 8u * s; };
+    auto kv_empty = [&](int s) { return bars + 8u * (kKvSlots + s); };
+    const uint32_t q_full = bars + 8u * (2 * kKvSlots);
+    auto s_full = [&](int g) { return bars + 8u * (2 * kKvSlots + 1 + g); };
+    auto p_ready = [&](int g) { return bars + 8u * (2 * kKvSlots + 3 + g); };
+    auto o_final = [&](int g) { return bars + 8u * (2 * kKvSlots + 5 + g); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * (2 * kKvSlots + 7));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_id();
+    const uint32_t lane = lane_id();
+
+    // Heaviest causal work first: later query pairs see more keys.
+    const int pair = p.pairs - 1 - static_cast<int>(blockIdx.x % p.pairs);
+    const int bh = static_cast<int>(blockIdx.x / p.pairs);
+    const int q0 = pair * 2 * kBlockQ;
+    const bool has_tile1 = q0 + kBlockQ < p.seq;
+    const int kv_end = p.causal ? min(p.seq, q0 + (has_tile1 ? 2 : 1) * kBlockQ) : p.seq;
+    const int n_blocks = (kv_end + kBlockKV - 1) / kBlockKV;
+    const bool single = p.seq <= kBlockKV;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kKvSlots; ++s) {
+            mbar_init(kv_full(s), 1);
+            mbar_init(kv_empty(s), 1);
+        }
+        mbar_init(q_full, 1);
+        for (int g = 0; g < 2; ++g) {
+            mbar_init(s_full(g), 1);
+            mbar_init(p_ready(g), 4);
+            mbar_init(o_final(g), 1);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 9) {
+        tmem_alloc<1>(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish<1>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 8) {
+        // ---------------- TMA producer (one thread) ----------------
+        if (lane == 0) {
+            tma_prefetch_desc(&map_q);
+            tma_prefetch_desc(&map_k);
+            tma_prefetch_desc(&map_v);
+            const int ntiles = has_tile1 ? 2 : 1;
+            mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
+            for (int g = 0; g < ntiles; ++g)
+                for (int x = 0; x < C::kBoxes; ++x)
+                    tma_load_3d(base + C::kQOffset + g * C::kTileBytes + x * 16384, &map_q, q_full,
+                                x * 64, q0 + g * kBlockQ, bh);
+            int slot = 0;
+            uint32_t phase = 0;
+            int issued = 0;
+            bool ok = true;
+            for (int j = 0; j < n_blocks && ok; ++j) {
+                for (int which = 0; which < 2; ++which) {  // K then V
+                    if (!mbar_wait(kv_empty(slot), phase ^ 1u, kFaultProducerWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = base + C::kKvOffset + slot * C::kTileBytes;
+                    mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
+                    for (int x = 0; x < C::kBoxes; ++x)
+                        tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
+                                    x * 64, j * kBlockKV, bh);
+                    ++issued;
+                    if (++slot == kKvSlots) {
+                        slot = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Let every issued load land before the CTA may exit: wait for the
+                // full-barrier phase of each of the last (up to kKvSlots) loads.
+                mbar_wait(q_full, 0, kFaultDrainWait, nullptr);
+                int s = slot;
+                uint32_t ph = phase;
+                for (int i = 0; i < min(issued, kKvSlots); ++i) {
+                    if (--s < 0) {
+                        s = kKvSlots - 1;
+                        ph ^= 1u;
+                    }
+                    mbar_wait(kv_full(s), ph, kFaultDrainWait, nullptr);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        bool ok = mbar_wait_warp(q_full, 0, kFaultAttnWait, abort_flag);
+        tc_fence_after();
+        const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
+        uint32_t pr_phase[2] = {0, 0};
+        int prev_v_slot = 0;
+        for (int j = 0; j < n_blocks && ok; ++j) {
+            const int k_slot = (2 * j) % kKvSlots;
+            const int v_slot = (2 * j + 1) % kKvSlots;
+            const uint32_t k_phase = static_cast<uint32_t>((2 * j) / kKvSlots) & 1u;
+            const uint32_t v_phase = static_cast<uint32_t>((2 * j + 1) / kKvSlots) & 1u;
+            if (!mbar_wait_warp(kv_full(k_slot), k_phase, kFaultAttnWait, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t k_addr = base + C::kKvOffset + k_slot * C::kTileBytes;
+            const uint32_t v_addr = base + C::kKvOffset + v_slot * C::kTileBytes;
+            // S0_j = Q0 K_j^T
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < kDPad / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    mma_f16_ss<1>(tmem + 0, sw128_desc(q_addr[0] + off, 16, 1024),
+                                  sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(s_full(0));
+            }
+            __syncwarp();
+            // PV1_{j-1}
+            if (j > 0 && has_tile1) {
+                if (!mbar_wait_warp(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                pr_phase[1] ^= 1u;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t pv_addr = base + C::kKvOffset + prev_v_slot * C::kTileBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockKV / 16; ++kk)
+                        mma_f16_ts(tmem + 256 + 128, tmem + 256 + kk * 8,
+                                   sw128_desc(pv_addr + kk * 2048, 16384, 1024), C::kIdescO,
+                                   (j - 1 > 0 || kk > 0) ? 1u : 0u);
+                }
+                __syncwarp();
+            }
+            if (j > 0 && lane == 0) mma_commit(kv_empty(prev_v_slot));
+            __syncwarp();
+            // S1_j = Q1 K_j^T
+            if (has_tile1) {
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < kDPad / 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        mma_f16_ss<1>(tmem + 256, sw128_desc(q_addr[1] + off, 16, 1024),
+                                      sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(s_full(1));
+                }
+                __syncwarp();
+            }
+            if (lane == 0) mma_commit(kv_empty(k_slot));
+            __syncwarp();
+            // PV0_j
+            if (!mbar_wait_warp(kv_full(v_slot), v_phase, kFaultAttnWait, abort_flag)) break;
+            if (!mbar_wait_warp(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
+            pr_phase[0] ^= 1u;
+            tc_fence_after();
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < kBlockKV / 16; ++kk)
+                    mma_f16_ts(tmem + 128, tmem + kk * 8, sw128_desc(v_addr + kk * 2048, 16384, 1024),
+                               C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
+                if (j == n_blocks - 1) mma_commit(o_final(0));
+            }
+            __syncwarp();
+            prev_v_slot = v_slot;
+            if (j == n_blocks - 1) {
+                // PV1_last
+                if (has_tile1) {
+                    if (!mbar_wait_warp(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                    pr_phase[1] ^= 1u;
+                    tc_fence_after();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int kk = 0; kk < kBlockKV / 16; ++kk)
+                            mma_f16_ts(tmem + 256 + 128, tmem + 256 + kk * 8,
+                                       sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
+                                       (j > 0 || kk > 0) ? 1u : 0u);
+                        mma_commit(o_final(1));
+                    }
+                    __syncwarp();
+                }
+                if (lane == 0) mma_commit(kv_empty(v_slot));
+                __syncwarp();
+            }
+        }
+    } else {
+        // ---------------- softmax warpgroups (warps 0-3: tile 0, 4-7: tile 1) ----------------
+        const int g = static_cast<int>(warp >> 2);
+        const uint32_t quarter = warp & 3u;
+        const int row_in_tile = static_cast<int>(quarter * 32 + lane);
+        const int q_row = q0 + g * kBlockQ + row_in_tile;
+        const uint32_t lane_bits = (quarter * 32u) << 16;
+        const uint32_t s_addr = tmem + lane_bits + 256u * g;
+        const uint32_t o_addr = s_addr + 128u;
+        const bool active = g == 0 || has_tile1;
+        float m_run = -INFINITY;  // running max, log2 units
+        float l_run = 0.0f;       // running sum of exp2(s - m_run)
+        bool ok = active;
+        for (int j = 0; j < n_blocks && ok; ++j) {
+            if (!mbar_wait_warp(s_full(g), static_cast<uint32_t>(j) & 1u, kFaultAttnWait, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(s_addr + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[i]) * p.scale_log2;
+            }
+            const int kv0 = j * kBlockKV;
+            // Keys past the sequence end, and (causal) keys after this query, are masked.
+            int limit = p.seq - kv0;
+            if (p.causal) limit = min(limit, q_row - kv0 + 1);
+            float m_blk = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) {
+                if (i >= limit) s[i] = -INFINITY;
+                m_blk = fmaxf(m_blk, s[i]);
+            }
+            const float m_new = fmaxf(m_run, m_blk);
+            // A row with no allowed key yet (only possible for padding rows) keeps m = -inf.
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            const float alpha = ex2(m_run - m_use);
+            float e_sum = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 128; ++i) {
+                s[i] = ex2(s[i] - m_use);
+                e_sum += s[i];
+            }
+            if (single) {
+                // One key block holds the whole row: normalise, then round.
+#pragma unroll
+                for (int i = 0; i < 128; ++i) s[i] = __fdiv_rn(s[i], e_sum);
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[i] = pack_half2(s[32 * c + 2 * i], s[32 * c + 2 * i + 1]);
+                tmem_st_32x32b_x16(s_addr + 16 * c, r);
+            }
+            // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp
+            // when any of its rows needs it (alpha == 1 rows multiply by one).
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                // Rescale the running output: PV_{j-1} has completed (in-order tcgen05).
+#pragma unroll
+                for (int c = 0; c < kDPad / 16; ++c) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(o_addr + 16 * c, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                    tmem_st_32x32b_x16(o_addr + 16 * c, r);
+                }
+            }
+            l_run = l_run * alpha + e_sum;
+            m_run = m_new;
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_ready(g));
+        }
+        if (ok && mbar_wait_warp(o_final(g), 0, kFaultAttnWait, abort_flag)) {
+            tc_fence_after();
+            const bool row_ok = q_row < p.seq;
+            float* orow = p.out + (static_cast<long long>(bh) * p.seq + q_row) * p.head_dim;
+#pragma unroll
+            for (int c = 0; c < kDPad / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(o_addr + 32 * c, r);
+                tmem_wait_ld();
+                if (row_ok) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int col = 32 * c + 4 * q;
+                        if (col < p.head_dim) {
+                            float4 v;
+                            v.x = __uint_as_float(r[4 * q]);
+                            v.y = __uint_as_float(r[4 * q + 1]);
+                            v.z = __uint_as_float(r[4 * q + 2]);
+                            v.w = __uint_as_float(r[4 * q + 3]);
+                            if (!single) {
+                                v.x = __fdiv_rn(v.x, l_run);
+                                v.y = __fdiv_rn(v.y, l_run);
+                                v.z = __fdiv_rn(v.z, l_run);
+                                v.w = __fdiv_rn(v.w, l_run);
+                            }
+                            if (p.out_vec4) {
+                                __stcs(reinterpret_cast<float4*>(orow + col), v);
+                            } else {
+                                orow[col] = v.x;
+                                orow[col + 1] = v.y;
+                                orow[col + 2] = v.z;
+                                orow[col + 3] = v.w;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        tmem_dealloc<1>(tmem, kTmemCols);
+    }
+}
+
+__global__ void repack_kernel(const uint16_t* src, uint16_t* dst, long long count) {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        dst[i] = src[i];
+}
+
+template <int kDPad>
+cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, int device,
+                   cudaStream_t stream) {
+    using Cc = Cfg<kDPad>;
+    static bool configured[host::kMaxDevices] = {};
+    auto kernel = attention_kernel<kDPad>;
+    if (!configured[device]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cc::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured[device] = true;
+    }
+    CUtensorMap mq, mk, mv;
+    const uint64_t dims[3] = {static_cast<uint64_t>(p.head_dim), static_cast<uint64_t>(p.seq),
+                              static_cast<uint64_t>(p.bh)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(p.head_dim) * 2,
+                                 static_cast<uint64_t>(p.head_dim) * 2 * static_cast<uint64_t>(p.seq)};
+    const uint32_t box[3] = {64, 128, 1};
+    if (!host::make_map_f16(&mq, q, 3, dims, strides, box) ||
+        !host::make_map_f16(&mk, k, 3, dims, strides, box) ||
+        !host::make_map_f16(&mv, v, 3, dims, strides, box)) {
+        return cudaErrorInvalidValue;
+    }
+    const long long grid = static_cast<long long>(p.bh) * p.pairs;
+    kernel<<<static_cast<unsigned>(grid), kThreads, Cc::kSmemBytes, stream>>>(mq, mk, mv, p);
+    return cudaSuccess;
+}
+
+inline cudaError_t attention_entry(const void* q, const void* k, const void* v, float* out, int batch,
+                                   int heads, int seq, int head_dim, float scale, int causal,
+                                   bool fixed_tile, cudaStream_t stream) {
+    if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return cudaErrorInvalidValue;
+    if (!fixed_tile) {
+        if (batch <= 0 || heads <= 0 || seq <= 0 ||
+            (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128) ||
+            (causal != 0 && causal != 1) || !(scale == scale) || scale == INFINITY ||
+            scale == -INFINITY) {
+            return cudaErrorInvalidValue;
+        }
+        const long long bh = static_cast<long long>(batch) * heads;
+        if (bh > INT_MAX || bh * ((seq + 255LL) / 256) > INT_MAX) return cudaErrorInvalidValue;
+        const size_t elems = static_cast<size_t>(bh) * static_cast<size_t>(seq) * head_dim;
+        if (host::ranges_overlap(out, elems * 4, q, elems * 2) ||
+            host::ranges_overlap(out, elems * 4, k, elems * 2) ||
+            host::ranges_overlap(out, elems * 4, v, elems * 2)) {
+            return cudaErrorInvalidValue;
+        }
+    }
+    int device = 0;
+    cudaError_t err = host::current_device(&device, nullptr);
+    if (err != cudaSuccess) return err;
+    static_cast<void>(cudaGetLastError());
+
+    Params p{};
+    p.seq = seq;
+    p.head_dim = head_dim;
+    p.pairs = (seq + 2 * kBlockQ - 1) / (2 * kBlockQ);
+    p.bh = batch * heads;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.causal = causal;
+    p.out = out;
+    p.out_vec4 = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+
+    // TMA needs 16-byte aligned bases; copy misaligned operands first.
+    const size_t elems = static_cast<size_t>(p.bh) * static_cast<size_t>(seq) * head_dim;
+    const void* src[3] = {q, k, v};
+    void* tmp[3] = {nullptr, nullptr, nullptr};
+    for (int i = 0; i < 3; ++i) {
+        if ((reinterpret_cast<uintptr_t>(src[i]) & 15u) != 0) {
+            err = cudaMallocAsync(&tmp[i], elems * 2, stream);
+            if (err != cudaSuccess) break;
+            repack_kernel<<<256, 256, 0, stream>>>(static_cast<const uint16_t*>(src[i]),
+                                                   static_cast<uint16_t*>(tmp[i]),
+                                                   static_cast<long long>(elems));
+            src[i] = tmp[i];
+        }
+    }
+    if (err == cudaSuccess) {
+        err = head_dim == 128 ? launch<128>(src[0], src[1], src[2], p, device, stream)
+                              : launch<64>(src[0], src[1], src[2], p, device, stream);
+    }
+    for (int i = 0; i < 3; ++i)
+        if (tmp[i] != nullptr) cudaFreeAsync(tmp[i], stream);
+    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
+
+}  // namespace attn
+}  // namespace tk

@@ -1,0 +1,407 @@
+// gemm.cuh — FP16 x FP16 -> FP32 row-major GEMM on sm_100a tensor cores.
+//
+// Replaces the SM7x WMMA/mma.sync kernel of ThunderKittens-SM7x
+// (src/gemm.cu:87-166) behind the same contract (src/gemm.cu:184-206).
+//
+// Data layout: A is M x K row-major (K contiguous: a K-major MMA operand), B is
+// K x N row-major (N contiguous: an MN-major operand), C is M x N row-major
+// FP32. Both operands are fetched by TMA in 128-byte swizzled boxes:
+//   A box  = 64 (K) x 128 (rows)        16 KiB, K-major SW128 canonical layout
+//   B box  = 64 (N) x  64 (K rows)       8 KiB, MN-major SW128 canonical layout
+// A stage holds one 64-deep K slice of the CTA's A rows and B columns. The ring
+// of stages is filled by one producer warp and drained by one MMA warp whose
+// elected lane issues tcgen05.mma (M = 128 per CTA, N = 256, K = 16) into a
+// TMEM accumulator. Two 256-column accumulators (all 512 TMEM columns) let the
+// four epilogue warps drain tile i (tcgen05.ld -> registers -> global) while
+// the tensor core runs tile i + 1.
+//
+// kCtaGroup = 2 pairs two CTAs of a cluster on one 256 x 256 tile
+// (tcgen05.mma.cta_group::2): each CTA loads its own 128 rows of A and its own
+// 128 columns of B (no multicast), the even CTA issues the MMAs for both, and
+// each CTA's TMEM receives its 128 rows of the 256 x 256 accumulator.
+//
+// The persistent grid walks output tiles in groups of kGroupM tile-rows so that
+// the CTAs resident at one time share A row-blocks and B column-blocks in L2.
+#pragma once
+
+#include "tk_ptx.cuh"
+
+namespace tk {
+namespace gemm {
+
+constexpr int kBlockM = 128;   // rows of C per CTA
+constexpr int kBlockN = 256;   // MMA N: columns of C per tile
+constexpr int kBlockK = 64;    // K per pipeline stage (one 128-byte swizzle row)
+constexpr int kMmaK = 16;      // K per tcgen05.mma (kind::f16)
+constexpr int kGroupM = 16;    // tile-rows per rasterisation group
+constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
+constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
+
+template <int kCtaGroup>
+struct Cfg {
+    static constexpr int kTileM = kBlockM * kCtaGroup;        // rows per tile (per cluster)
+    static constexpr int kBCols = kBlockN / kCtaGroup;        // B columns loaded per CTA
+    static constexpr int kABytes = kBlockM * kBlockK * 2;     // 16 KiB
+    static constexpr int kBBytes = kBlockK * kBCols * 2;      // 32 or 16 KiB
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = kCtaGroup == 1 ? 4 : 6;
+    static constexpr int kBarrierBytes = 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + align slack
+    static constexpr uint32_t kIdesc = idesc_f16_f32(kBlockM * kCtaGroup, kBlockN, 0, 1);
+};
+
+struct Params {
+    int m, n, k;
+    float* c;
+    long long ldc;
+    bool c_vec4;        // c 16-byte aligned and ldc % 4 == 0
+    int m_tiles, n_tiles, k_blocks;
+    int num_tiles;
+    // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
+    float* partial;     // [m][n_tiles][2] (max, sum), or null
+};
+
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int* tm, int* tn) {
+    const int per_group = kGroupM * n_tiles;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int rows = min(kGroupM, m_tiles - first_m);
+    const int r = t - group * per_group;
+    *tm = first_m + r % rows;
+    *tn = r / rows;
+}
+
+struct OpSumG {
+    __device__ __forceinline__ static float apply(float lo, float hi) { return lo + hi; }
+};
+struct OpMaxG {
+    __device__ __forceinline__ static float apply(float lo, float hi) { return lo > hi ? lo : hi; }
+};
+
+// Canonical balanced tree over 16 consecutive values.
+template <class Op>
+__device__ __forceinline__ float tree16(const float* x) {
+    const float q0 = Op::apply(Op::apply(x[0], x[1]), Op::apply(x[2], x[3]));
+    const float q1 = Op::apply(Op::apply(x[4], x[5]), Op::apply(x[6], x[7]));
+    const float q2 = Op::apply(Op::apply(x[8], x[9]), Op::apply(x[10], x[11]));
+    const float q3 = Op::apply(Op::apply(x[12], x[13]), Op::apply(x[14], x[15]));
+    return Op::apply(Op::apply(q0, q1), Op::apply(q2, q3));
+}
+
+// Level-by-level pairwise reduction of g[0..count) (count <= 16), odd last
+// element carried up; fully unrolled so g stays in registers.
+template <class Op>
+__device__ __forceinline__ float pairwise16(float (&g)[16], int count) {
+#pragma unroll
+    for (int width = 16; width > 1; width >>= 1) {
+#pragma unroll
+        for (int i = 0; i < width / 2; ++i) {
+            const bool has_low = 2 * i < count;
+            const bool has_high = 2 * i + 1 < count;
+            if (has_low) g[i] = has_high ? Op::apply(g[2 * i], g[2 * i + 1]) : g[2 * i];
+        }
+        count = (count + 1) >> 1;
+    }
+    return g[0];
+}
+
+template <int kCtaGroup, bool kRowStats>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const Params p) {
+    using C = Cfg<kCtaGroup>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_base);
+
+    const uint32_t barriers = base + C::kStages * C::kStageBytes;
+    auto full_bar = [&](int s) { return barriers + 8u * s; };
+    auto empty_bar = [&](int s) { return barriers + 8u * (C::kStages + s); };
+    auto tfull_bar = [&](int b) { return barriers + 8u * (2 * C::kStages + b); };
+    auto tempty_bar = [&](int b) { return barriers + 8u * (2 * C::kStages + 2 + b); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kStages * C::kStageBytes + 8 * (2 * C::kStages + 4));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_id();
+    const uint32_t lane = lane_id();
+    const uint32_t rank = kCtaGroup == 2 ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
+    const int cluster_id = static_cast<int>(blockIdx.x) / kCtaGroup;
+    const int num_clusters = static_cast<int>(gridDim.x) / kCtaGroup;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 4 * kCtaGroup);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+    }
+    if (warp == 5) {
+        tmem_alloc<kCtaGroup>(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish<kCtaGroup>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (kCtaGroup == 2) cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 4) {
+        // ---------------- producer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = 0;
+        bool ok = true;
+        const uint32_t leader_full0 = kCtaGroup == 2 ? mapa_shared(full_bar(0), 0) : full_bar(0);
+        for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+            int tm, tn;
+            tile_coords(t, p.m_tiles, p.n_tiles, &tm, &tn);
+            const int row0 = tm * C::kTileM + static_cast<int>(rank) * kBlockM;
+            const int col0 = tn * kBlockN + static_cast<int>(rank) * C::kBCols;
+            for (int kb = 0; kb < p.k_blocks; ++kb) {
+                if (!mbar_wait_warp(empty_bar(stage), phase ^ 1u, kFaultProducerWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    const uint32_t a_dst = base + stage * C::kStageBytes;
+                    const uint32_t b_dst = a_dst + C::kABytes;
+                    if constexpr (kCtaGroup == 1) {
+                        mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
+                        tma_load_2d(a_dst, &map_a, full_bar(stage), kb * kBlockK, row0);
+#pragma unroll
+                        for (int j = 0; j < C::kBCols / 64; ++j)
+                            tma_load_2d(b_dst + j * 8192, &map_b, full_bar(stage), col0 + j * 64,
+                                        kb * kBlockK);
+                    } else {
+                        if (leader) mbar_arrive_expect_tx(full_bar(stage), 2 * C::kStageBytes);
+                        const uint32_t fb = leader_full0 + 8u * stage;
+                        tma_load_2d_pair(a_dst, &map_a, fb, kb * kBlockK, row0);
+#pragma unroll
+                        for (int j = 0; j < C::kBCols / 64; ++j)
+                            tma_load_2d_pair(b_dst + j * 8192, &map_b, fb, col0 + j * 64,
+                                             kb * kBlockK);
+                    }
+                }
+                __syncwarp();
+                ++issued;
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+        }
+        // Drain: the last loads issued by this CTA must land before it may exit.
+        if (!ok && leader) {
+            int s = stage;
+            uint32_t ph = phase;
+            for (int i = 0; i < min(issued, C::kStages); ++i) {
+                if (--s < 0) {
+                    s = C::kStages - 1;
+                    ph ^= 1u;
+                }
+                mbar_wait_warp(full_bar(s), ph, kFaultDrainWait, nullptr);
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer (leader CTA) ----------------
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+                if (!mbar_wait_warp(tempty_bar(acc), acc_phase ^ 1u, kFaultMmaWait, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBlockN);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait_warp(full_bar(stage), phase, kFaultMmaWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_addr = base + stage * C::kStageBytes;
+                        const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+                        for (int kk = 0; kk < kBlockK / kMmaK; ++kk) {
+                            const uint64_t a_desc = sw128_desc(a_addr + kk * 32, 16, 1024);
+                            const uint64_t b_desc = sw128_desc(b_addr + kk * 2048, 8192, 1024);
+                            mma_f16_ss<kCtaGroup>(d_tmem, a_desc, b_desc, C::kIdesc,
+                                                  (kb | kk) != 0 ? 1u : 0u);
+                        }
+                        if constexpr (kCtaGroup == 1) {
+                            mma_commit(empty_bar(stage));
+                        } else {
+                            mma_commit_pair(empty_bar(stage), 0x3);
+                        }
+                    }
+                    __syncwarp();
+                    if (++stage == C::kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                if (lane == 0) {
+                    if constexpr (kCtaGroup == 1) {
+                        mma_commit(tfull_bar(acc));
+                    } else {
+                        mma_commit_pair(tfull_bar(acc), 0x3);
+                    }
+                }
+                __syncwarp();
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 0-3: TMEM -> registers -> global ----------------
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        const uint32_t tempty_remote =
+            kCtaGroup == 2 ? mapa_shared(tempty_bar(0), 0) : tempty_bar(0);
+        for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
+            int tm, tn;
+            tile_coords(t, p.m_tiles, p.n_tiles, &tm, &tn);
+            if (!mbar_wait_warp(tfull_bar(acc), acc_phase, kFaultEpilogueWait, abort_flag)) break;
+            tc_fence_after();
+            const long long row =
+                static_cast<long long>(tm) * C::kTileM + rank * kBlockM + warp * 32 + lane;
+            const int col_base = tn * kBlockN;
+            const bool row_ok = row < p.m;
+            float* crow = p.c + row * p.ldc;
+            const uint32_t t_addr = tmem_base + ((warp * 32u) << 16) + static_cast<uint32_t>(acc * kBlockN);
+            float gmax[16], gsum[16];
+#pragma unroll
+            for (int chunk = 0; chunk < kBlockN / 32; ++chunk) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_addr + chunk * 32, r);
+                tmem_wait_ld();
+                const int col0 = col_base + chunk * 32;
+                if (row_ok) {
+                    if (p.c_vec4) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            if (col0 + q * 4 < p.n) {
+                                float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                                *reinterpret_cast<float4*>(crow + col0 + q * 4) = v;
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q)
+                            if (col0 + q < p.n) crow[col0 + q] = __uint_as_float(r[q]);
+                    }
+                }
+                if constexpr (kRowStats) {
+                    float x[32];
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) x[q] = __uint_as_float(r[q]);
+                    gmax[2 * chunk] = tree16<OpMaxG>(x);
+                    gmax[2 * chunk + 1] = tree16<OpMaxG>(x + 16);
+                    gsum[2 * chunk] = tree16<OpSumG>(x);
+                    gsum[2 * chunk + 1] = tree16<OpSumG>(x + 16);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if constexpr (kCtaGroup == 1) {
+                    mbar_arrive(tempty_bar(acc));
+                } else {
+                    mbar_arrive_cluster(tempty_remote + 8u * acc);
+                }
+            }
+            if constexpr (kRowStats) {
+                if (row_ok) {
+                    const int groups = min(16, (p.n - col_base) / 16);
+                    const float mx = pairwise16<OpMaxG>(gmax, groups);
+                    const float sm = pairwise16<OpSumG>(gsum, groups);
+                    float2* dst = reinterpret_cast<float2*>(p.partial) + (row * p.n_tiles + tn);
+                    *dst = make_float2(mx, sm);
+                }
+            }
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (kCtaGroup == 2) cluster_sync();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc<kCtaGroup>(tmem_base, kTmemCols);
+    }
+}
+
+// Finishing pass of the fused row statistics: per row, combine the per-tile
+// partials in tile order with the same pairwise rule (binary-counter form: a
+// stack of complete power-of-two blocks, merged right to left at the end, which
+// equals the level-by-level pairing with the odd element carried up).
+__global__ void rowstats_finish_kernel(const float2* partial, int m, int n_tiles, float* row_max,
+                                       float* row_sum) {
+    const long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (row >= m) return;
+    float smax[32], ssum[32];
+    int ssize[32];
+    int top = 0;
+    const float2* src = partial + row * n_tiles;
+    for (int i = 0; i < n_tiles; ++i) {
+        float2 v = src[i];
+        float vmax = v.x, vsum = v.y;
+        int size = 1;
+        while (top > 0 && ssize[top - 1] == size) {
+            --top;
+            vmax = OpMaxG::apply(smax[top], vmax);
+            vsum = OpSumG::apply(ssum[top], vsum);
+            size *= 2;
+        }
+        smax[top] = vmax;
+        ssum[top] = vsum;
+        ssize[top] = size;
+        ++top;
+    }
+    float vmax = smax[top - 1], vsum = ssum[top - 1];
+    for (int i = top - 2; i >= 0; --i) {
+        vmax = OpMaxG::apply(smax[i], vmax);
+        vsum = OpSumG::apply(ssum[i], vsum);
+    }
+    row_max[row] = vmax;
+    row_sum[row] = vsum;
+}
+
+// Copies a binary16 matrix with an arbitrary leading dimension / alignment into
+// a dense 16-byte-aligned buffer (rows x cols, leading dimension cols) so that
+// TMA can read it. Used only when the caller's operand cannot be described by a
+// tensor map (row pitch not a multiple of 16 bytes or a misaligned base).
+__global__ void repack_f16_kernel(const uint16_t* src, long long ld, uint16_t* dst, long long rows,
+                                  int cols) {
+    const long long total = rows * cols;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / cols;
+        const long long c = i - r * cols;
+        dst[i] = src[r * ld + c];
+    }
+}
+
+}  // namespace gemm
+}  // namespace tk

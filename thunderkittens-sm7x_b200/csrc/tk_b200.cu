@@ -1,0 +1,339 @@
+// tk_b200.cu — the library's single translation unit and its C ABI
+// (include/tk_b200.h). Argument validation and error-state rules follow
+// ThunderKittens-SM7x src/gemm.cu:184-206 and src/attention.cu:62-86:
+// invalid arguments return cudaErrorInvalidValue before anything else happens
+// (no launch, outputs untouched, the pending CUDA error left in place); a valid
+// call clears the pending error, enqueues, and returns cudaGetLastError().
+
+#include "tk_b200.h"
+
+#include <climits>
+#include <cstdint>
+
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "rowops.cuh"
+#include "tk_host.cuh"
+
+namespace {
+
+using tk::host::current_device;
+
+constexpr int kAbiVersion = 100;
+
+// ---------------------------------------------------------------------------
+// Tile row operations
+// ---------------------------------------------------------------------------
+
+template <int kOps, bool kVec>
+void launch_rowops_typed(const float* tiles, size_t n_tiles, float* s, float* m, float* sm, float* cs,
+                         int sm_count, cudaStream_t stream) {
+    static int blocks_per_sm = 0;
+    if (blocks_per_sm == 0) {
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &occ, tk::rowops::tile_row_ops_kernel<kOps, kVec>, tk::rowops::kThreads, 0) !=
+                cudaSuccess ||
+            occ <= 0) {
+            occ = 4;
+        }
+        blocks_per_sm = occ;
+    }
+    const size_t tiles_per_block = (tk::rowops::kThreads / 32) * tk::rowops::kTilesPerWarpStep;
+    const size_t needed = (n_tiles + tiles_per_block - 1) / tiles_per_block;
+    const size_t cap = static_cast<size_t>(sm_count) * blocks_per_sm;
+    const unsigned grid = static_cast<unsigned>(needed < cap ? needed : cap);
+    tk::rowops::tile_row_ops_kernel<kOps, kVec>
+        <<<grid, tk::rowops::kThreads, 0, stream>>>(tiles, n_tiles, s, m, sm, cs);
+}
+
+template <int kOps>
+void launch_rowops_ops(bool vec, const float* tiles, size_t n_tiles, float* s, float* m, float* sm,
+                       float* cs, int sm_count, cudaStream_t stream) {
+    if (vec) {
+        launch_rowops_typed<kOps, true>(tiles, n_tiles, s, m, sm, cs, sm_count, stream);
+    } else {
+        launch_rowops_typed<kOps, false>(tiles, n_tiles, s, m, sm, cs, sm_count, stream);
+    }
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+cudaError_t rowops(const float* tiles, size_t n_tiles, float* sum_out, float* max_out,
+                   float* softmax_out, float* causal_out, bool allow_inplace, cudaStream_t stream) {
+    if (tiles == nullptr || (sum_out == nullptr && max_out == nullptr && softmax_out == nullptr &&
+                             causal_out == nullptr)) {
+        return cudaErrorInvalidValue;
+    }
+    if (n_tiles > SIZE_MAX / 1024) return cudaErrorInvalidValue;
+    const float* outs[4] = {sum_out, max_out, softmax_out, causal_out};
+    const size_t out_bytes[4] = {n_tiles * 64, n_tiles * 64, n_tiles * 1024, n_tiles * 1024};
+    const size_t in_bytes = n_tiles * 1024;
+    for (int i = 0; i < 4; ++i) {
+        if (outs[i] == nullptr) continue;
+        if (!aligned(outs[i], 4)) return cudaErrorInvalidValue;
+        if (tk::host::ranges_overlap(outs[i], out_bytes[i], tiles, in_bytes) &&
+            !(allow_inplace && static_cast<const void*>(outs[i]) == static_cast<const void*>(tiles) &&
+              out_bytes[i] == in_bytes)) {
+            return cudaErrorInvalidValue;
+        }
+        for (int j = i + 1; j < 4; ++j) {
+            if (outs[j] != nullptr && tk::host::ranges_overlap(outs[i], out_bytes[i], outs[j], out_bytes[j]))
+                return cudaErrorInvalidValue;
+        }
+    }
+    if (!aligned(tiles, 4)) return cudaErrorInvalidValue;
+    int sm_count = 0;
+    cudaError_t err = current_device(nullptr, &sm_count);
+    if (err != cudaSuccess) return err;
+    static_cast<void>(cudaGetLastError());
+    if (n_tiles == 0) return cudaSuccess;
+    bool vec = aligned(tiles, 16);
+    for (int i = 0; i < 4; ++i)
+        if (outs[i] != nullptr) vec = vec && aligned(outs[i], 16);
+    const int ops = (sum_out ? tk::rowops::kSum : 0) | (max_out ? tk::rowops::kMax : 0) |
+                    (softmax_out ? tk::rowops::kSoftmax : 0) | (causal_out ? tk::rowops::kCausal : 0);
+    switch (ops) {
+#define TK_ROWOPS_CASE(N)                                                                              \
+    case N:                                                                                            \
+        launch_rowops_ops<N>(vec, tiles, n_tiles, sum_out, max_out, softmax_out, causal_out, sm_count, \
+                             stream);                                                                  \
+        break;
+        TK_ROWOPS_CASE(1) TK_ROWOPS_CASE(2) TK_ROWOPS_CASE(3) TK_ROWOPS_CASE(4) TK_ROWOPS_CASE(5)
+        TK_ROWOPS_CASE(6) TK_ROWOPS_CASE(7) TK_ROWOPS_CASE(8) TK_ROWOPS_CASE(9) TK_ROWOPS_CASE(10)
+        TK_ROWOPS_CASE(11) TK_ROWOPS_CASE(12) TK_ROWOPS_CASE(13) TK_ROWOPS_CASE(14) TK_ROWOPS_CASE(15)
+#undef TK_ROWOPS_CASE
+        default: break;
+    }
+    return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// GEMM
+// ---------------------------------------------------------------------------
+
+int g_gemm_cta_group_override = 0;  // 0 = choose by problem size
+
+template <int kCtaGroup, bool kRowStats>
+cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
+                               int device, int sm_count, cudaStream_t stream) {
+    using Cfg = tk::gemm::Cfg<kCtaGroup>;
+    auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kRowStats>;
+    static bool configured[tk::host::kMaxDevices] = {};
+    if (!configured[device]) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured[device] = true;
+    }
+    const int max_clusters = sm_count / kCtaGroup;
+    const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(clusters * kCtaGroup));
+    cfg.blockDim = dim3(tk::gemm::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCtaGroup;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
+}
+
+cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b, int ldb, float* c,
+                      int ldc, float* row_max, float* row_sum, cudaStream_t stream) {
+    const bool stats = row_max != nullptr || row_sum != nullptr;
+    if (a == nullptr || b == nullptr || c == nullptr || m <= 0 || n <= 0 || k <= 0 || m % 16 != 0 ||
+        n % 16 != 0 || k % 16 != 0 || lda < k || ldb < n || ldc < n) {
+        return cudaErrorInvalidValue;
+    }
+    if (stats && (row_max == nullptr || row_sum == nullptr ||
+                  tk::host::ranges_overlap(row_max, sizeof(float) * m, row_sum, sizeof(float) * m))) {
+        return cudaErrorInvalidValue;
+    }
+    int sm_count = 0, device = 0;
+    cudaError_t err = current_device(&device, &sm_count);
+    if (err != cudaSuccess) return err;
+    static_cast<void>(cudaGetLastError());
+
+    // Operands whose rows TMA cannot address (row pitch not a multiple of 16
+    // bytes, or a base that is not 16-byte aligned) are first copied into dense
+    // stream-ordered buffers.
+    const void* a_use = a;
+    const void* b_use = b;
+    long long lda_use = lda, ldb_use = ldb;
+    void* a_tmp = nullptr;
+    void* b_tmp = nullptr;
+    if (!aligned(a, 16) || lda % 8 != 0) {
+        err = cudaMallocAsync(&a_tmp, static_cast<size_t>(m) * k * 2, stream);
+        if (err != cudaSuccess) return err;
+        tk::gemm::repack_f16_kernel<<<1024, 256, 0, stream>>>(static_cast<const uint16_t*>(a), lda,
+                                                              static_cast<uint16_t*>(a_tmp), m, k);
+        a_use = a_tmp;
+        lda_use = k;
+    }
+    if (!aligned(b, 16) || ldb % 8 != 0) {
+        err = cudaMallocAsync(&b_tmp, static_cast<size_t>(k) * n * 2, stream);
+        if (err != cudaSuccess) {
+            if (a_tmp) cudaFreeAsync(a_tmp, stream);
+            return err;
+        }
+        tk::gemm::repack_f16_kernel<<<1024, 256, 0, stream>>>(static_cast<const uint16_t*>(b), ldb,
+                                                              static_cast<uint16_t*>(b_tmp), k, n);
+        b_use = b_tmp;
+        ldb_use = n;
+    }
+
+    int cta_group = g_gemm_cta_group_override;
+    if (cta_group == 0) {
+        const long long big_tiles = ((m + 255LL) / 256) * ((n + 255LL) / 256);
+        cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
+    }
+
+    CUtensorMap ma, mb;
+    const uint64_t a_dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t a_strides[1] = {static_cast<uint64_t>(lda_use) * 2};
+    const uint32_t a_box[2] = {64, 128};
+    const uint64_t b_dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
+    const uint64_t b_strides[1] = {static_cast<uint64_t>(ldb_use) * 2};
+    const uint32_t b_box[2] = {64, 64};
+    if (!tk::host::make_map_f16(&ma, a_use, 2, a_dims, a_strides, a_box) ||
+        !tk::host::make_map_f16(&mb, b_use, 2, b_dims, b_strides, b_box)) {
+        if (a_tmp) cudaFreeAsync(a_tmp, stream);
+        if (b_tmp) cudaFreeAsync(b_tmp, stream);
+        return cudaErrorInvalidValue;
+    }
+
+    tk::gemm::Params p{};
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.c = c;
+    p.ldc = ldc;
+    p.c_vec4 = aligned(c, 16) && ldc % 4 == 0;
+    const int tile_m = tk::gemm::kBlockM * cta_group;
+    p.m_tiles = (m + tile_m - 1) / tile_m;
+    p.n_tiles = (n + tk::gemm::kBlockN - 1) / tk::gemm::kBlockN;
+    p.k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
+    const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
+    if (tiles > INT_MAX) {
+        if (a_tmp) cudaFreeAsync(a_tmp, stream);
+        if (b_tmp) cudaFreeAsync(b_tmp, stream);
+        return cudaErrorInvalidValue;
+    }
+    p.num_tiles = static_cast<int>(tiles);
+
+    float* partial = nullptr;
+    if (stats) {
+        err = cudaMallocAsync(reinterpret_cast<void**>(&partial),
+                              static_cast<size_t>(m) * p.n_tiles * sizeof(float2), stream);
+        if (err != cudaSuccess) {
+            if (a_tmp) cudaFreeAsync(a_tmp, stream);
+            if (b_tmp) cudaFreeAsync(b_tmp, stream);
+            return err;
+        }
+    }
+    p.partial = partial;
+
+    if (cta_group == 2) {
+        err = stats ? launch_gemm_kernel<2, true>(ma, mb, p, device, sm_count, stream)
+                    : launch_gemm_kernel<2, false>(ma, mb, p, device, sm_count, stream);
+    } else {
+        err = stats ? launch_gemm_kernel<1, true>(ma, mb, p, device, sm_count, stream)
+                    : launch_gemm_kernel<1, false>(ma, mb, p, device, sm_count, stream);
+    }
+    if (stats && err == cudaSuccess) {
+        tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(
+            reinterpret_cast<const float2*>(partial), m, p.n_tiles, row_max, row_sum);
+    }
+    if (partial) cudaFreeAsync(partial, stream);
+    if (a_tmp) cudaFreeAsync(a_tmp, stream);
+    if (b_tmp) cudaFreeAsync(b_tmp, stream);
+    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" {
+
+cudaError_t tk_gemm_f16_f16_f32_nn(int m, int n, int k, const void* a, int lda, const void* b,
+                                   int ldb, float* c, int ldc, cudaStream_t stream) {
+    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, nullptr, nullptr, stream);
+}
+
+cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const void* a, int lda,
+                                            const void* b, int ldb, float* c, int ldc,
+                                            float* row_max, float* row_sum, cudaStream_t stream) {
+    if (row_max == nullptr || row_sum == nullptr) return cudaErrorInvalidValue;
+    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream);
+}
+
+int tk_gemm_set_cta_group(int cta_group) {
+    const int prev = g_gemm_cta_group_override;
+    if (cta_group >= 0 && cta_group <= 2) g_gemm_cta_group_override = cta_group;
+    return prev;
+}
+
+cudaError_t tk_tile_row_sum_f32(const float* tiles, size_t n_tiles, float* out, cudaStream_t stream) {
+    return rowops(tiles, n_tiles, out, nullptr, nullptr, nullptr, false, stream);
+}
+
+cudaError_t tk_tile_row_max_f32(const float* tiles, size_t n_tiles, float* out, cudaStream_t stream) {
+    return rowops(tiles, n_tiles, nullptr, out, nullptr, nullptr, false, stream);
+}
+
+cudaError_t tk_tile_row_softmax_f32(const float* tiles, size_t n_tiles, float* out,
+                                    cudaStream_t stream) {
+    return rowops(tiles, n_tiles, nullptr, nullptr, out, nullptr, true, stream);
+}
+
+cudaError_t tk_tile_row_softmax_causal_f32(const float* tiles, size_t n_tiles, float* out,
+                                           cudaStream_t stream) {
+    return rowops(tiles, n_tiles, nullptr, nullptr, nullptr, out, true, stream);
+}
+
+cudaError_t tk_tile_row_ops_f32(const float* tiles, size_t n_tiles, float* row_sum, float* row_max,
+                                float* softmax, float* softmax_causal, cudaStream_t stream) {
+    return rowops(tiles, n_tiles, row_sum, row_max, softmax, softmax_causal, false, stream);
+}
+
+cudaError_t tk_attention_forward_16x16(const void* q, const void* k, const void* v, float* out,
+                                       cudaStream_t stream) {
+    return tk::attn::attention_entry(q, k, v, out, 1, 1, 16, 16, 0.25f, 0, true, stream);
+}
+
+cudaError_t tk_attention_forward_16x16_causal(const void* q, const void* k, const void* v,
+                                              float* out, cudaStream_t stream) {
+    return tk::attn::attention_entry(q, k, v, out, 1, 1, 16, 16, 0.25f, 1, true, stream);
+}
+
+cudaError_t tk_attention_forward_f16(const void* q, const void* k, const void* v, float* out,
+                                     int batch, int heads, int seq, int head_dim, float scale,
+                                     int causal, cudaStream_t stream) {
+    return tk::attn::attention_entry(q, k, v, out, batch, heads, seq, head_dim, scale, causal, false,
+                                     stream);
+}
+
+cudaError_t tk_device_status(uint32_t* status, int clear) {
+    if (status == nullptr) return cudaErrorInvalidValue;
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return err;
+    unsigned int value = 0;
+    err = cudaMemcpyFromSymbol(&value, tk::g_tk_status, sizeof(value));
+    if (err != cudaSuccess) return err;
+    if (clear) {
+        const unsigned int zero = 0;
+        err = cudaMemcpyToSymbol(tk::g_tk_status, &zero, sizeof(zero));
+        if (err != cudaSuccess) return err;
+    }
+    *status = value;
+    return cudaSuccess;
+}
+
+int tk_abi_version(void) { return kAbiVersion; }
+
+}  // extern "C"
