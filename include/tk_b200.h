@@ -67,6 +67,38 @@ TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const vo
                                                    float* c, int ldc, float* row_max,
                                                    float* row_sum, cudaStream_t stream);
 
+/* Largest m * ceil(n / 256) accepted by tk_gemm_f16_f16_f32_nn_rowstats_noalloc:
+ * the number of (max, sum) float pairs its built-in scratch holds (4 MiB). */
+#define TK_GEMM_ROWSTATS_NOALLOC_MAX_PARTIALS (1u << 19)
+
+/* No counterpart in the reference. The fused row-statistics GEMM above for
+ * callers that must not allocate device memory: code that runs where cudaMalloc
+ * and the stream-ordered allocator are off limits (a custom or arena allocator
+ * that owns all device memory, a host process that forbids allocation after
+ * start-up, or real-time paths where an allocation could block). It computes
+ * exactly what tk_gemm_f16_f16_f32_nn_rowstats computes, but takes its per-tile
+ * partials from a fixed 4 MiB array compiled into the library instead of
+ * allocating them, and calls no allocation routine at all.
+ *   - Limit: m * ceil(n / 256) must not exceed TK_GEMM_ROWSTATS_NOALLOC_MAX_PARTIALS
+ *     (for example m = 8192 with n up to 16384); larger problems return
+ *     cudaErrorNotSupported before anything is enqueued.
+ *   - A and B must be TMA-addressable as given (16-byte aligned base pointers,
+ *     lda and ldb multiples of 8); other layouts would need a repacking copy and
+ *     return cudaErrorNotSupported. Other invalid arguments return
+ *     cudaErrorInvalidValue, as for the other GEMM entry points.
+ *   - The array lives on every GPU that loads the library until the process
+ *     exits. The first call on a device looks up its device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before capturing the stream into a CUDA graph.
+ *   - All calls share the array and each call overwrites the partials it uses
+ *     before reading them. Calls whose kernels overlap on the GPU (different
+ *     streams, or concurrent host threads on one device) race on it: order them
+ *     on one stream or serialise them. */
+TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowstats_noalloc(int m, int n, int k, const void* a,
+                                                           int lda, const void* b, int ldb,
+                                                           float* c, int ldc, float* row_max,
+                                                           float* row_sum, cudaStream_t stream);
+
 /* Tuning knob, no counterpart in the reference (whose tile choice is the fixed
  * rule of src/gemm.cu:50-57): 0 = choose by problem size (default), 1 = one CTA
  * per 128 x 256 tile, 2 = CTA pairs on 256 x 256 tiles. Process-wide; returns

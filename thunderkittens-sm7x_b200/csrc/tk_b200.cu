@@ -9,6 +9,7 @@
 
 #include <climits>
 #include <cstdint>
+#include <mutex>
 
 #include "attention.cuh"
 #include "gemm.cuh"
@@ -256,6 +257,93 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Fused row-statistics GEMM without allocation
+// ---------------------------------------------------------------------------
+
+// Scratch of tk_gemm_f16_f16_f32_nn_rowstats_noalloc: one (max, sum) pair per
+// (row, 256-column tile). Every GPU that loads the library holds it until exit.
+// In host code this name only stands for the array: its device address comes
+// from cudaGetSymbolAddress, looked up once per device below.
+static __device__ __align__(256) float2 g_rowstats_noalloc_scratch[TK_GEMM_ROWSTATS_NOALLOC_MAX_PARTIALS];
+
+std::mutex g_noalloc_mutex;
+float2* g_noalloc_scratch_ptr[tk::host::kMaxDevices] = {};
+
+// Device address of the scratch array on `device`, which must be current.
+cudaError_t noalloc_scratch(int device, float2** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (g_noalloc_scratch_ptr[device] == nullptr) {
+        void* ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress(&ptr, g_rowstats_noalloc_scratch);
+        if (err != cudaSuccess) return err;
+        g_noalloc_scratch_ptr[device] = static_cast<float2*>(ptr);
+    }
+    *out = g_noalloc_scratch_ptr[device];
+    return cudaSuccess;
+}
+
+cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, const void* b, int ldb,
+                                  float* c, int ldc, float* row_max, float* row_sum,
+                                  cudaStream_t stream) {
+    if (a == nullptr || b == nullptr || c == nullptr || row_max == nullptr || row_sum == nullptr ||
+        m <= 0 || n <= 0 || k <= 0 || m % 16 != 0 || n % 16 != 0 || k % 16 != 0 || lda < k ||
+        ldb < n || ldc < n ||
+        tk::host::ranges_overlap(row_max, sizeof(float) * m, row_sum, sizeof(float) * m)) {
+        return cudaErrorInvalidValue;
+    }
+    const long long n_tiles = (n + tk::gemm::kBlockN - 1) / tk::gemm::kBlockN;
+    if (static_cast<long long>(m) * n_tiles > static_cast<long long>(TK_GEMM_ROWSTATS_NOALLOC_MAX_PARTIALS))
+        return cudaErrorNotSupported;  // more partials than the built-in scratch holds
+    if (!aligned(a, 16) || lda % 8 != 0 || !aligned(b, 16) || ldb % 8 != 0)
+        return cudaErrorNotSupported;  // would need a repacking copy, i.e. an allocation
+    int sm_count = 0, device = 0;
+    cudaError_t err = current_device(&device, &sm_count);
+    if (err != cudaSuccess) return err;
+    static_cast<void>(cudaGetLastError());
+    float2* scratch = nullptr;
+    err = noalloc_scratch(device, &scratch);
+    if (err != cudaSuccess) return err;
+
+    int cta_group = g_gemm_cta_group_override;
+    if (cta_group == 0) {
+        const long long big_tiles = ((m + 255LL) / 256) * ((n + 255LL) / 256);
+        cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
+    }
+    CUtensorMap ma, mb;
+    const uint64_t a_dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t a_strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t a_box[2] = {64, 128};
+    const uint64_t b_dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
+    const uint64_t b_strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t b_box[2] = {64, 64};
+    if (!tk::host::make_map_f16(&ma, a, 2, a_dims, a_strides, a_box) ||
+        !tk::host::make_map_f16(&mb, b, 2, b_dims, b_strides, b_box)) {
+        return cudaErrorInvalidValue;
+    }
+    tk::gemm::Params p{};
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.c = c;
+    p.ldc = ldc;
+    p.c_vec4 = aligned(c, 16) && ldc % 4 == 0;
+    const int tile_m = tk::gemm::kBlockM * cta_group;
+    p.m_tiles = (m + tile_m - 1) / tile_m;
+    p.n_tiles = static_cast<int>(n_tiles);
+    p.k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
+    p.num_tiles = p.m_tiles * p.n_tiles;
+    // Every (row < m, tile) pair is written by the GEMM epilogue before the
+    // finishing pass reads it, so nothing left by an earlier call is ever used.
+    p.partial = reinterpret_cast<float*>(scratch);
+    err = cta_group == 2 ? launch_gemm_kernel<2, true>(ma, mb, p, device, sm_count, stream)
+                         : launch_gemm_kernel<1, true>(ma, mb, p, device, sm_count, stream);
+    if (err != cudaSuccess) return err;
+    tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(scratch, m, p.n_tiles, row_max,
+                                                                         row_sum);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 extern "C" {
@@ -270,6 +358,13 @@ cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const void* a, 
                                             float* row_max, float* row_sum, cudaStream_t stream) {
     if (row_max == nullptr || row_sum == nullptr) return cudaErrorInvalidValue;
     return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream);
+}
+
+cudaError_t tk_gemm_f16_f16_f32_nn_rowstats_noalloc(int m, int n, int k, const void* a, int lda,
+                                                    const void* b, int ldb, float* c, int ldc,
+                                                    float* row_max, float* row_sum,
+                                                    cudaStream_t stream) {
+    return gemm_rowstats_noalloc(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream);
 }
 
 int tk_gemm_set_cta_group(int cta_group) {

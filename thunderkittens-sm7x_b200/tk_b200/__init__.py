@@ -24,12 +24,15 @@ LIB_PATH = os.path.join(HERE, "libtk_b200.so")
 CUDA_SUCCESS = 0
 CUDA_ERROR_INVALID_VALUE = 1
 CUDA_ERROR_INVALID_DEVICE_FUNCTION = 98
+CUDA_ERROR_NOT_SUPPORTED = 801
 
 # Every symbol include/tk_b200.h declares, with its ctypes signature.
 _VP, _I, _SZ, _F = C.c_void_p, C.c_int, C.c_size_t, C.c_float
 SIGNATURES = {
     "tk_gemm_f16_f16_f32_nn": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP]),
     "tk_gemm_f16_f16_f32_nn_rowstats": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _VP, _VP]),
+    "tk_gemm_f16_f16_f32_nn_rowstats_noalloc": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _VP,
+                                                     _VP]),
     "tk_gemm_set_cta_group": (_I, [_I]),
     "tk_tile_row_sum_f32": (_I, [_VP, _SZ, _VP, _VP]),
     "tk_tile_row_max_f32": (_I, [_VP, _SZ, _VP, _VP]),
