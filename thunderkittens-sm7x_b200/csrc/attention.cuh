@@ -44,6 +44,13 @@ constexpr int kBlockQ = 128;
 constexpr int kBlockKV = 128;
 constexpr int kKvSlots = 4;
 constexpr uint32_t kTmemCols = 512;
+// One score in kFmaExpEvery takes the FMA-pipe exponential (the rest use MUFU);
+// 0 sends every score to MUFU. Measured on B200 at [8,32,4096,128]: every 4 / 8 /
+// 16 / none gave 973 / 1032 / 1008 / 1040 TFLOP/s, so MUFU alone is the default.
+#ifndef TK_ATTN_FMA_EXP_EVERY
+#define TK_ATTN_FMA_EXP_EVERY 0
+#endif
+constexpr int kFmaExpEvery = TK_ATTN_FMA_EXP_EVERY;
 
 template <int kDPad>
 struct Cfg {
@@ -74,9 +81,107 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, available to move a share of the exponentials off the MUFU
+// unit (kFmaExpEvery). Cody-Waite split x = n + f with n = rint(x), f in [-0.5, 0.5];
+// 2^f from a degree-5 polynomial (least-squares fit on Chebyshev nodes of
+// [-0.5, 0.5], constant term pinned to 1; max relative error 1.8e-7, i.e. within
+// ~1.5 ulp of FP32); 2^n applied by adding n to the exponent field. Inputs are
+// clamped at -125 so the result stays a normal float; anything that small rounds
+// to 0 in binary16.
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fmaxf(x, -125.0f);
+    const float shifter = 12582912.0f;  // 1.5 * 2^23: x + shifter holds rint(x) in its low bits
+    const float t = x + shifter;
+    const float n = t - shifter;
+    const float f = x - n;
+    float p = 1.3218672e-3f;
+    p = fmaf(p, f, 9.6716983e-3f);
+    p = fmaf(p, f, 5.5508930e-2f);
+    p = fmaf(p, f, 2.4022238e-1f);
+    p = fmaf(p, f, 6.9314688e-1f);
+    p = fmaf(p, f, 1.0f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Score of column `col` in log2 units for the masked / non-positive-scale path:
+// scaled when the scale is not positive (then the exponent argument uses factor
+// 1), -inf when the key is masked.
+__device__ __forceinline__ float score_slow(uint32_t raw, int col, int limit, bool pos_scale, float c_in) {
+    float v = __uint_as_float(raw);
+    if (!pos_scale) v *= c_in;
+    return col >= limit ? -INFINITY : v;
+}
+
+// Row max over the 128 scores of this thread's row (S in TMEM at s_addr), read as
+// two pairs of 32-column chunks. kFast: no masked key and a positive scale.
+template <bool kFast>
+__device__ __forceinline__ float score_row_max(uint32_t s_addr, int limit, bool pos_scale, float c_in) {
+    float mx[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) mx[t] = -INFINITY;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(s_addr + 64 * half, ra);
+        tmem_ld_32x32b_x32(s_addr + 64 * half + 32, rb);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float va = kFast ? __uint_as_float(ra[i]) : score_slow(ra[i], 64 * half + i, limit, pos_scale, c_in);
+            const float vb = kFast ? __uint_as_float(rb[i]) : score_slow(rb[i], 64 * half + 32 + i, limit, pos_scale, c_in);
+            mx[i & 7] = fmaxf(mx[i & 7], fmaxf(va, vb));
+        }
+    }
+    return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+}
+
+// Exponentials 2^(s * c_eff - m) of the row, chunk by chunk, with the next chunk's
+// TMEM load in flight while the current one is computed. One score in eight goes
+// to the FMA pipe (exp2_fma), the rest to MUFU. kMode 0: write binary16 P (over
+// the S columns already consumed) and return the sum; 1: only return the sum;
+// 2: write binary16 P / norm (exact normalise-then-round of a single key block).
+template <bool kFast, int kMode>
+__device__ __forceinline__ float score_row_exp(uint32_t s_addr, int limit, bool pos_scale, float c_in,
+                                               float c_eff, float neg_m, float norm) {
+    float acc[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
+    uint32_t r[2][32];
+    tmem_ld_32x32b_x32(s_addr, r[0]);
+    tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        if (c < 3) tmem_ld_32x32b_x32(s_addr + 32 * (c + 1), r[(c + 1) & 1]);
+        float e[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float v = kFast ? __uint_as_float(r[c & 1][i]) : score_slow(r[c & 1][i], 32 * c + i, limit, pos_scale, c_in);
+            const float arg = fmaf(v, c_eff, neg_m);
+            e[i] = (kFmaExpEvery > 0 && i % (kFmaExpEvery > 0 ? kFmaExpEvery : 1) == kFmaExpEvery - 1)
+                       ? exp2_fma(arg)
+                       : ex2(arg);
+            acc[i & 7] += e[i];
+        }
+        if constexpr (kMode != 1) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                if constexpr (kMode == 2) {
+                    pk[i] = pack_half2(__fdiv_rn(e[2 * i], norm), __fdiv_rn(e[2 * i + 1], norm));
+                } else {
+                    pk[i] = pack_half2(e[2 * i], e[2 * i + 1]);
+                }
+            }
+            tmem_st_32x32b_x16(s_addr + 16 * c, pk);
+        }
+        if (c < 3) tmem_wait_ld();
+    }
+    return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
 }
 
 template <int kDPad>
@@ -295,46 +400,45 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
-            float s[128];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(s_addr + 32 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 32; ++i) s[32 * c + i] = __uint_as_float(r[i]) * p.scale_log2;
-            }
             const int kv0 = j * kBlockKV;
             // Keys past the sequence end, and (causal) keys after this query, are masked.
             int limit = p.seq - kv0;
             if (p.causal) limit = min(limit, q_row - kv0 + 1);
-            float m_blk = -INFINITY;
-#pragma unroll
-            for (int i = 0; i < 128; ++i) {
-                if (i >= limit) s[i] = -INFINITY;
-                m_blk = fmaxf(m_blk, s[i]);
-            }
+            const bool need_mask = __any_sync(0xffffffffu, limit < kBlockKV);
+            // Scores in log2 units are s * c. For c > 0 the max of the raw scores is
+            // scaled once and each exponent argument is a single FMA; otherwise the
+            // scores are scaled first. Blocks with no masked key take a branch-free
+            // path (the choice is warp-uniform).
+            const float c_in = p.scale_log2;
+            const bool pos_scale = c_in > 0.0f;
+            const float c_eff = pos_scale ? c_in : 1.0f;
+            const bool fast = pos_scale && !need_mask;
+            const float m_raw = fast ? score_row_max<true>(s_addr, limit, pos_scale, c_in)
+                                     : score_row_max<false>(s_addr, limit, pos_scale, c_in);
+            const float m_blk = m_raw * c_eff;
             const float m_new = fmaxf(m_run, m_blk);
-            // A row with no allowed key yet (only possible for padding rows) keeps m = -inf.
-            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-            const float alpha = ex2(m_run - m_use);
-            float e_sum = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 128; ++i) {
-                s[i] = ex2(s[i] - m_use);
-                e_sum += s[i];
-            }
+            // The reference point only moves when the max grows by more than 8 (so
+            // unnormalised probabilities stay <= 2^8); otherwise O needs no rescale.
+            // The first block always sets it, so a single-block row uses its exact max.
+            float m_use = m_new > m_run + 8.0f ? m_new : m_run;
+            // A row with no allowed key yet (only padding rows) keeps a finite point.
+            if (m_use == -INFINITY) m_use = 0.0f;
+            const float alpha = m_use == m_run ? 1.0f : ex2(m_run - m_use);
+            const float neg_m = -m_use;
+            float e_sum;
             if (single) {
-                // One key block holds the whole row: normalise, then round.
-#pragma unroll
-                for (int i = 0; i < 128; ++i) s[i] = __fdiv_rn(s[i], e_sum);
-            }
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) r[i] = pack_half2(s[32 * c + 2 * i], s[32 * c + 2 * i + 1]);
-                tmem_st_32x32b_x16(s_addr + 16 * c, r);
+                // One key block holds the whole row: sum first, then normalise and
+                // round (the exponentials are recomputed from the intact S).
+                e_sum = fast ? score_row_exp<true, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
+                             : score_row_exp<false, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                if (fast) {
+                    score_row_exp<true, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                } else {
+                    score_row_exp<false, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                }
+            } else {
+                e_sum = fast ? score_row_exp<true, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
+                             : score_row_exp<false, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
             }
             // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp
             // when any of its rows needs it (alpha == 1 rows multiply by one).
@@ -351,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             l_run = l_run * alpha + e_sum;
-            m_run = m_new;
+            m_run = m_use;
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
