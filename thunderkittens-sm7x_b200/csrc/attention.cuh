@@ -584,7 +584,7 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
     void* tmp[3] = {nullptr, nullptr, nullptr};
     for (int i = 0; i < 3; ++i) {
         if ((reinterpret_cast<uintptr_t>(src[i]) & 15u) != 0) {
-            err = cudaMallocAsync(&tmp[i], elems * 2, stream);
+            err = host::scratch_alloc(&tmp[i], elems * 2, device, stream);
             if (err != cudaSuccess) break;
             repack_kernel<<<256, 256, 0, stream>>>(static_cast<const uint16_t*>(src[i]),
                                                    static_cast<uint16_t*>(tmp[i]),

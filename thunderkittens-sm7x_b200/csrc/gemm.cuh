@@ -56,7 +56,12 @@ struct Params {
     long long ldc;
     bool c_vec4;        // c 16-byte aligned and ldc % 4 == 0
     int m_tiles, n_tiles, k_blocks;
-    int num_tiles;
+    int num_tiles;      // m_tiles * n_tiles * k_splits work units
+    // Split-K (small-M problems): unit t covers K blocks [ks * kb_per_split, ...)
+    // and writes its partial C to ws[ks][m][n] (dense); splitk_reduce_kernel then
+    // sums the splits in order into C. k_splits == 1 writes C directly.
+    int k_splits, kb_per_split;
+    float* ws;
     // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
     float* partial;     // [m][n_tiles][2] (max, sum), or null
 };
@@ -69,6 +74,14 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
     const int r = t - group * per_group;
     *tm = first_m + r % rows;
     *tn = r / rows;
+}
+
+// Output tile and K-block range of work unit t.
+__device__ __forceinline__ void work_coords(int t, const Params& p, int* tm, int* tn, int* kb0, int* kb1) {
+    const int ks = t % p.k_splits;
+    tile_coords(t / p.k_splits, p.m_tiles, p.n_tiles, tm, tn);
+    *kb0 = ks * p.kb_per_split;
+    *kb1 = min(*kb0 + p.kb_per_split, p.k_blocks);
 }
 
 struct OpSumG {
@@ -164,11 +177,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         const uint32_t leader_full0 = kCtaGroup == 2 ? mapa_shared(full_bar(0), 0) : full_bar(0);
         for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
-            int tm, tn;
-            tile_coords(t, p.m_tiles, p.n_tiles, &tm, &tn);
+            int tm, tn, kb0, kb1;
+            work_coords(t, p, &tm, &tn, &kb0, &kb1);
             const int row0 = tm * C::kTileM + static_cast<int>(rank) * kBlockM;
             const int col0 = tn * kBlockN + static_cast<int>(rank) * C::kBCols;
-            for (int kb = 0; kb < p.k_blocks; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait_warp(empty_bar(stage), phase ^ 1u, kFaultProducerWait, abort_flag)) {
                     ok = false;
                     break;
@@ -224,8 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
                 if (!mbar_wait_warp(tempty_bar(acc), acc_phase ^ 1u, kFaultMmaWait, abort_flag)) break;
                 tc_fence_after();
+                int tm, tn, kb0, kb1;
+                work_coords(t, p, &tm, &tn, &kb0, &kb1);
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBlockN);
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_warp(full_bar(stage), phase, kFaultMmaWait, abort_flag)) {
                         ok = false;
                         break;
@@ -239,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const uint64_t a_desc = sw128_desc(a_addr + kk * 32, 16, 1024);
                             const uint64_t b_desc = sw128_desc(b_addr + kk * 2048, 8192, 1024);
                             mma_f16_ss<kCtaGroup>(d_tmem, a_desc, b_desc, C::kIdesc,
-                                                  (kb | kk) != 0 ? 1u : 0u);
+                                                  (kb > kb0 || kk > 0) ? 1u : 0u);
                         }
                         if constexpr (kCtaGroup == 1) {
                             mma_commit(empty_bar(stage));
@@ -275,15 +290,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tempty_remote =
             kCtaGroup == 2 ? mapa_shared(tempty_bar(0), 0) : tempty_bar(0);
         for (int t = cluster_id; t < p.num_tiles; t += num_clusters) {
-            int tm, tn;
-            tile_coords(t, p.m_tiles, p.n_tiles, &tm, &tn);
+            int tm, tn, kb0, kb1;
+            work_coords(t, p, &tm, &tn, &kb0, &kb1);
             if (!mbar_wait_warp(tfull_bar(acc), acc_phase, kFaultEpilogueWait, abort_flag)) break;
             tc_fence_after();
             const long long row =
                 static_cast<long long>(tm) * C::kTileM + rank * kBlockM + warp * 32 + lane;
             const int col_base = tn * kBlockN;
             const bool row_ok = row < p.m;
-            float* crow = p.c + row * p.ldc;
+            const bool split = p.k_splits > 1;
+            float* crow = split ? p.ws + (static_cast<long long>(t % p.k_splits) * p.m + row) * p.n
+                                : p.c + row * p.ldc;
+            const bool vec4 = split || p.c_vec4;
             const uint32_t t_addr = tmem_base + ((warp * 32u) << 16) + static_cast<uint32_t>(acc * kBlockN);
             float gmax[16], gsum[16];
 #pragma unroll
@@ -293,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_wait_ld();
                 const int col0 = col_base + chunk * 32;
                 if (row_ok) {
-                    if (p.c_vec4) {
+                    if (vec4) {
 #pragma unroll
                         for (int q = 0; q < 8; ++q) {
                             if (col0 + q * 4 < p.n) {
@@ -386,6 +404,36 @@ __global__ void rowstats_finish_kernel(const float2* partial, int m, int n_tiles
     }
     row_max[row] = vmax;
     row_sum[row] = vsum;
+}
+
+// Sums the split-K partials ws[0..splits)[m][n] in split order into C (ldc).
+__global__ void splitk_reduce_kernel(const float* ws, int splits, int m, int n, float* c, long long ldc,
+                                     bool c_vec4) {
+    const long long quads = static_cast<long long>(m) * (n / 4);
+    const long long plane = static_cast<long long>(m) * n;
+    for (long long q = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; q < quads;
+         q += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = q / (n / 4);
+        const int col = static_cast<int>(q - row * (n / 4)) * 4;
+        const float* src = ws + row * n + col;
+        float4 acc = *reinterpret_cast<const float4*>(src);
+        for (int s = 1; s < splits; ++s) {
+            const float4 v = *reinterpret_cast<const float4*>(src + s * plane);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        float* dst = c + row * ldc + col;
+        if (c_vec4) {
+            *reinterpret_cast<float4*>(dst) = acc;
+        } else {
+            dst[0] = acc.x;
+            dst[1] = acc.y;
+            dst[2] = acc.z;
+            dst[3] = acc.w;
+        }
+    }
 }
 
 // Copies a binary16 matrix with an arbitrary leading dimension / alignment into

@@ -169,7 +169,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     void* a_tmp = nullptr;
     void* b_tmp = nullptr;
     if (!aligned(a, 16) || lda % 8 != 0) {
-        err = cudaMallocAsync(&a_tmp, static_cast<size_t>(m) * k * 2, stream);
+        err = tk::host::scratch_alloc(&a_tmp, static_cast<size_t>(m) * k * 2, device, stream);
         if (err != cudaSuccess) return err;
         tk::gemm::repack_f16_kernel<<<1024, 256, 0, stream>>>(static_cast<const uint16_t*>(a), lda,
                                                               static_cast<uint16_t*>(a_tmp), m, k);
@@ -177,7 +177,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         lda_use = k;
     }
     if (!aligned(b, 16) || ldb % 8 != 0) {
-        err = cudaMallocAsync(&b_tmp, static_cast<size_t>(k) * n * 2, stream);
+        err = tk::host::scratch_alloc(&b_tmp, static_cast<size_t>(k) * n * 2, device, stream);
         if (err != cudaSuccess) {
             if (a_tmp) cudaFreeAsync(a_tmp, stream);
             return err;
@@ -225,12 +225,35 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         if (b_tmp) cudaFreeAsync(b_tmp, stream);
         return cudaErrorInvalidValue;
     }
-    p.num_tiles = static_cast<int>(tiles);
+    // Split K when the output has too few tiles to occupy the GPU (decode-shaped
+    // problems): at least 4 K blocks per split, partials at most 64 MiB.
+    p.k_splits = 1;
+    p.kb_per_split = p.k_blocks;
+    if (!stats && tiles < sm_count / 2 && p.k_blocks >= 8) {
+        int splits = static_cast<int>(sm_count / tiles);
+        if (splits > p.k_blocks / 4) splits = p.k_blocks / 4;
+        while (splits > 1 && static_cast<long long>(splits) * m * n * 4 > (64LL << 20)) --splits;
+        if (splits > 1) {
+            p.kb_per_split = (p.k_blocks + splits - 1) / splits;
+            p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
+        }
+    }
+    p.num_tiles = static_cast<int>(tiles) * p.k_splits;
+    p.ws = nullptr;
+    if (p.k_splits > 1) {
+        err = tk::host::scratch_alloc(reinterpret_cast<void**>(&p.ws),
+                                      static_cast<size_t>(p.k_splits) * m * n * sizeof(float), device, stream);
+        if (err != cudaSuccess) {
+            if (a_tmp) cudaFreeAsync(a_tmp, stream);
+            if (b_tmp) cudaFreeAsync(b_tmp, stream);
+            return err;
+        }
+    }
 
     float* partial = nullptr;
     if (stats) {
-        err = cudaMallocAsync(reinterpret_cast<void**>(&partial),
-                              static_cast<size_t>(m) * p.n_tiles * sizeof(float2), stream);
+        err = tk::host::scratch_alloc(reinterpret_cast<void**>(&partial),
+                                      static_cast<size_t>(m) * p.n_tiles * sizeof(float2), device, stream);
         if (err != cudaSuccess) {
             if (a_tmp) cudaFreeAsync(a_tmp, stream);
             if (b_tmp) cudaFreeAsync(b_tmp, stream);
@@ -249,6 +272,14 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     if (stats && err == cudaSuccess) {
         tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(
             reinterpret_cast<const float2*>(partial), m, p.n_tiles, row_max, row_sum);
+    }
+    if (p.k_splits > 1) {
+        if (err == cudaSuccess) {
+            const long long quads = static_cast<long long>(m) * (n / 4);
+            const int blocks = static_cast<int>(quads / 256 + 1 < 4 * sm_count ? quads / 256 + 1 : 4 * sm_count);
+            tk::gemm::splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.ws, p.k_splits, m, n, c, ldc, p.c_vec4);
+        }
+        cudaFreeAsync(p.ws, stream);
     }
     if (partial) cudaFreeAsync(partial, stream);
     if (a_tmp) cudaFreeAsync(a_tmp, stream);
@@ -333,6 +364,9 @@ cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, c
     p.n_tiles = static_cast<int>(n_tiles);
     p.k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
     p.num_tiles = p.m_tiles * p.n_tiles;
+    p.k_splits = 1;
+    p.kb_per_split = p.k_blocks;
+    p.ws = nullptr;
     // Every (row < m, tile) pair is written by the GEMM epilogue before the
     // finishing pass reads it, so nothing left by an earlier call is ever used.
     p.partial = reinterpret_cast<float*>(scratch);

@@ -98,6 +98,37 @@ inline bool make_map_f16(CUtensorMap* map, const void* base, int rank, const uin
     return r == CUDA_SUCCESS;
 }
 
+// Stream-ordered scratch from a private per-device memory pool that keeps its
+// memory (release threshold = max), so repeated calls reuse the same pages instead
+// of mapping and unmapping them around every call. The pool is the library's own;
+// the process's default pool is left untouched.
+inline cudaError_t scratch_alloc(void** ptr, size_t bytes, int device, cudaStream_t stream) {
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    static std::mutex mu;
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (pools[device] == nullptr) {
+            cudaMemPoolProps props{};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = device;
+            cudaMemPool_t created = nullptr;
+            cudaError_t err = cudaMemPoolCreate(&created, &props);
+            if (err != cudaSuccess) return err;
+            uint64_t keep = UINT64_MAX;
+            err = cudaMemPoolSetAttribute(created, cudaMemPoolAttrReleaseThreshold, &keep);
+            if (err != cudaSuccess) {
+                static_cast<void>(cudaMemPoolDestroy(created));
+                return err;
+            }
+            pools[device] = created;
+        }
+        pool = pools[device];
+    }
+    return cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
+}
+
 inline bool ranges_overlap(const void* a, size_t a_bytes, const void* b, size_t b_bytes) {
     const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
     return a0 < b0 + b_bytes && b0 < a0 + a_bytes;
