@@ -60,8 +60,8 @@ TK_API cudaError_t tk_gemm_f16_f16_f32_nn(int m, int n, int k, const void* a, in
  * Generalises examples/gemm_row_stats.cu:17-40 from one 16x16 tile to full rows.
  * row_max and row_sum hold m floats each and must not overlap C or each other.
  * The per-tile partials (m * ceil(n / 256) float pairs) live in a scratch
- * buffer taken from the stream-ordered allocator (cudaMallocAsync) and returned
- * with cudaFreeAsync on the same stream. */
+ * buffer taken stream-ordered (cudaMallocFromPoolAsync) from a memory pool the
+ * library creates per device and returned with cudaFreeAsync on the same stream. */
 TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const void* a,
                                                    int lda, const void* b, int ldb,
                                                    float* c, int ldc, float* row_max,
@@ -162,6 +162,16 @@ TK_API cudaError_t tk_attention_forward_f16(const void* q, const void* k, const 
                                             float* out, int batch, int heads, int seq,
                                             int head_dim, float scale, int causal,
                                             cudaStream_t stream);
+
+/* Grouped-query attention, a generalisation the reference rules out (README.md:35-36):
+ * Q and out are [batch, heads_q, seq, head_dim], K and V are [batch, heads_kv,
+ * seq, head_dim]; query head h attends with key/value head h / (heads_q /
+ * heads_kv). heads_q must be a multiple of heads_kv; everything else as
+ * tk_attention_forward_f16 (which is the heads_kv == heads_q case). */
+TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, const void* v,
+                                                float* out, int batch, int heads_q, int heads_kv,
+                                                int seq, int head_dim, float scale, int causal,
+                                                cudaStream_t stream);
 
 /* ---- status ------------------------------------------------------------------ */
 

@@ -130,3 +130,10 @@ def test_valid_call_without_gpu_reports_an_error_not_a_crash():
         pytest.skip("a GPU is present")
     code = tk_b200.lib().tk_tile_row_sum_f32(FAKE, 4, FAKE * 8, None)
     assert code not in (0, INVALID)
+
+
+def test_gqa_invalid_arguments():
+    lib = tk_b200.lib()
+    # heads_q not a multiple of heads_kv, and zero key/value heads
+    assert lib.tk_attention_forward_gqa_f16(FAKE, FAKE, FAKE, 1 << 40, 1, 6, 4, 64, 64, 0.125, 0, None) == INVALID
+    assert lib.tk_attention_forward_gqa_f16(FAKE, FAKE, FAKE, 1 << 40, 1, 6, 0, 64, 64, 0.125, 0, None) == INVALID

@@ -129,3 +129,25 @@ def test_large_8x32x4096x128_sampled(causal):
     rng = np.random.default_rng(1)
     rows = np.unique(np.concatenate([[0, 4095], rng.integers(0, 4096, 30)]))
     general_case(8, 32, 4096, 128, causal, seed=4, rows=rows, pairs=[0, 77, 180, 255])
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("heads_q,heads_kv", [(8, 2), (4, 1), (6, 3)])
+def test_grouped_query_attention(heads_q, heads_kv, causal):
+    """Query head h attends with key/value head h / (heads_q / heads_kv)."""
+    b, s, d = 2, 300, 64
+    group = heads_q // heads_kv
+    q, _, _ = oracle.gen_qkv_normal(40 + heads_q, 1.0, b * heads_q * s * d)
+    _, k, v = oracle.gen_qkv_normal(50 + heads_kv, 1.0, b * heads_kv * s * d)
+    out = torch.full((b * heads_q * s * d,), float("nan"), device="cuda")
+    tq, tk_, tv = dev(q), dev(k), dev(v)
+    scale = 1.0 / math.sqrt(d)
+    assert tk_b200.attention_gqa_raw(tq, tk_, tv, out, b, heads_q, heads_kv, s, d, scale, causal) == 0
+    got = host(out).reshape(b * heads_q, s, d)
+    qs = q.reshape(b * heads_q, s, d)
+    ks, vs = k.reshape(b * heads_kv, s, d), v.reshape(b * heads_kv, s, d)
+    for bh in range(b * heads_q):
+        kv = (bh // heads_q) * heads_kv + (bh % heads_q) // group
+        want = oracle.attention_ref(qs[bh], ks[kv], vs[kv], s, d, scale, causal)
+        bound = oracle.attention_bound(vs[kv], s, d)
+        assert np.all(np.abs(got[bh] - want) <= bound[None, :]), bh

@@ -68,7 +68,10 @@ struct Params {
     int seq;           // S
     int head_dim;      // D (valid output columns)
     int pairs;         // ceil(S / 256): query-tile pairs per (batch, head)
-    int bh;            // B * H
+    int bh;            // B * H (query heads)
+    int heads_q;       // H
+    int group;         // query heads per key/value head (1 = multi-head, >1 = GQA)
+    int heads_kv;      // H / group
     float scale_log2;  // scale * log2(e)
     int causal;
     float* out;
@@ -209,6 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Heaviest causal work first: later query pairs see more keys.
     const int pair = p.pairs - 1 - static_cast<int>(blockIdx.x % p.pairs);
     const int bh = static_cast<int>(blockIdx.x / p.pairs);
+    // Key/value slice: query head h of batch b reads key/value head h / group.
+    const int bh_kv = (bh / p.heads_q) * p.heads_kv + (bh % p.heads_q) / p.group;
     const int q0 = pair * 2 * kBlockQ;
     const bool has_tile1 = q0 + kBlockQ < p.seq;
     const int kv_end = p.causal ? min(p.seq, q0 + (has_tile1 ? 2 : 1) * kBlockQ) : p.seq;
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
                     for (int x = 0; x < C::kBoxes; ++x)
                         tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
-                                    x * 64, j * kBlockKV, bh);
+                                    x * 64, j * kBlockKV, bh_kv);
                     ++issued;
                     if (++slot == kKvSlots) {
                         slot = 0;
@@ -530,12 +535,14 @@ cudaError_t launch(const void* q, const void* k, const void* v, const Params& p,
     CUtensorMap mq, mk, mv;
     const uint64_t dims[3] = {static_cast<uint64_t>(p.head_dim), static_cast<uint64_t>(p.seq),
                               static_cast<uint64_t>(p.bh)};
+    const uint64_t dims_kv[3] = {static_cast<uint64_t>(p.head_dim), static_cast<uint64_t>(p.seq),
+                                 static_cast<uint64_t>(p.bh / p.group)};
     const uint64_t strides[2] = {static_cast<uint64_t>(p.head_dim) * 2,
                                  static_cast<uint64_t>(p.head_dim) * 2 * static_cast<uint64_t>(p.seq)};
     const uint32_t box[3] = {64, 128, 1};
     if (!host::make_map_f16(&mq, q, 3, dims, strides, box) ||
-        !host::make_map_f16(&mk, k, 3, dims, strides, box) ||
-        !host::make_map_f16(&mv, v, 3, dims, strides, box)) {
+        !host::make_map_f16(&mk, k, 3, dims_kv, strides, box) ||
+        !host::make_map_f16(&mv, v, 3, dims_kv, strides, box)) {
         return cudaErrorInvalidValue;
     }
     const long long grid = static_cast<long long>(p.bh) * p.pairs;
@@ -544,11 +551,11 @@ cudaError_t launch(const void* q, const void* k, const void* v, const Params& p,
 }
 
 inline cudaError_t attention_entry(const void* q, const void* k, const void* v, float* out, int batch,
-                                   int heads, int seq, int head_dim, float scale, int causal,
+                                   int heads, int heads_kv, int seq, int head_dim, float scale, int causal,
                                    bool fixed_tile, cudaStream_t stream) {
     if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return cudaErrorInvalidValue;
     if (!fixed_tile) {
-        if (batch <= 0 || heads <= 0 || seq <= 0 ||
+        if (batch <= 0 || heads <= 0 || heads_kv <= 0 || heads % heads_kv != 0 || seq <= 0 ||
             (head_dim != 16 && head_dim != 32 && head_dim != 64 && head_dim != 128) ||
             (causal != 0 && causal != 1) || !(scale == scale) || scale == INFINITY ||
             scale == -INFINITY) {
@@ -557,9 +564,10 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
         const long long bh = static_cast<long long>(batch) * heads;
         if (bh > INT_MAX || bh * ((seq + 255LL) / 256) > INT_MAX) return cudaErrorInvalidValue;
         const size_t elems = static_cast<size_t>(bh) * static_cast<size_t>(seq) * head_dim;
+        const size_t elems_kv = elems / static_cast<size_t>(heads / heads_kv);
         if (host::ranges_overlap(out, elems * 4, q, elems * 2) ||
-            host::ranges_overlap(out, elems * 4, k, elems * 2) ||
-            host::ranges_overlap(out, elems * 4, v, elems * 2)) {
+            host::ranges_overlap(out, elems * 4, k, elems_kv * 2) ||
+            host::ranges_overlap(out, elems * 4, v, elems_kv * 2)) {
             return cudaErrorInvalidValue;
         }
     }
@@ -573,17 +581,22 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
     p.head_dim = head_dim;
     p.pairs = (seq + 2 * kBlockQ - 1) / (2 * kBlockQ);
     p.bh = batch * heads;
+    p.heads_q = heads;
+    p.heads_kv = heads_kv;
+    p.group = heads / heads_kv;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.causal = causal;
     p.out = out;
     p.out_vec4 = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
 
     // TMA needs 16-byte aligned bases; copy misaligned operands first.
-    const size_t elems = static_cast<size_t>(p.bh) * static_cast<size_t>(seq) * head_dim;
+    const size_t elems_q = static_cast<size_t>(p.bh) * static_cast<size_t>(seq) * head_dim;
+    const size_t elems_kv = elems_q / static_cast<size_t>(p.group);
     const void* src[3] = {q, k, v};
     void* tmp[3] = {nullptr, nullptr, nullptr};
     for (int i = 0; i < 3; ++i) {
         if ((reinterpret_cast<uintptr_t>(src[i]) & 15u) != 0) {
+            const size_t elems = i == 0 ? elems_q : elems_kv;
             err = host::scratch_alloc(&tmp[i], elems * 2, device, stream);
             if (err != cudaSuccess) break;
             repack_kernel<<<256, 256, 0, stream>>>(static_cast<const uint16_t*>(src[i]),

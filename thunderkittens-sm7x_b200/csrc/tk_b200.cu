@@ -432,19 +432,26 @@ cudaError_t tk_tile_row_ops_f32(const float* tiles, size_t n_tiles, float* row_s
 
 cudaError_t tk_attention_forward_16x16(const void* q, const void* k, const void* v, float* out,
                                        cudaStream_t stream) {
-    return tk::attn::attention_entry(q, k, v, out, 1, 1, 16, 16, 0.25f, 0, true, stream);
+    return tk::attn::attention_entry(q, k, v, out, 1, 1, 1, 16, 16, 0.25f, 0, true, stream);
 }
 
 cudaError_t tk_attention_forward_16x16_causal(const void* q, const void* k, const void* v,
                                               float* out, cudaStream_t stream) {
-    return tk::attn::attention_entry(q, k, v, out, 1, 1, 16, 16, 0.25f, 1, true, stream);
+    return tk::attn::attention_entry(q, k, v, out, 1, 1, 1, 16, 16, 0.25f, 1, true, stream);
 }
 
 cudaError_t tk_attention_forward_f16(const void* q, const void* k, const void* v, float* out,
                                      int batch, int heads, int seq, int head_dim, float scale,
                                      int causal, cudaStream_t stream) {
-    return tk::attn::attention_entry(q, k, v, out, batch, heads, seq, head_dim, scale, causal, false,
+    return tk::attn::attention_entry(q, k, v, out, batch, heads, heads, seq, head_dim, scale, causal, false,
                                      stream);
+}
+
+cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, const void* v, float* out,
+                                         int batch, int heads_q, int heads_kv, int seq, int head_dim,
+                                         float scale, int causal, cudaStream_t stream) {
+    return tk::attn::attention_entry(q, k, v, out, batch, heads_q, heads_kv, seq, head_dim, scale, causal,
+                                     false, stream);
 }
 
 cudaError_t tk_device_status(uint32_t* status, int clear) {

@@ -42,6 +42,7 @@ SIGNATURES = {
     "tk_attention_forward_16x16": (_I, [_VP, _VP, _VP, _VP, _VP]),
     "tk_attention_forward_16x16_causal": (_I, [_VP, _VP, _VP, _VP, _VP]),
     "tk_attention_forward_f16": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP]),
+    "tk_attention_forward_gqa_f16": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tk_device_status": (_I, [C.POINTER(C.c_uint32), _I]),
     "tk_abi_version": (_I, []),
 }
@@ -120,6 +121,11 @@ def attention_16x16_raw(q, k, v, out, causal=False, stream=None) -> int:
 def attention_raw(q, k, v, out, batch, heads, seq, head_dim, scale, causal, stream=None) -> int:
     return lib().tk_attention_forward_f16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), batch, heads, seq,
                                           head_dim, float(scale), 1 if causal else 0, _stream(stream))
+
+
+def attention_gqa_raw(q, k, v, out, batch, heads_q, heads_kv, seq, head_dim, scale, causal, stream=None) -> int:
+    return lib().tk_attention_forward_gqa_f16(_ptr(q), _ptr(k), _ptr(v), _ptr(out), batch, heads_q, heads_kv,
+                                              seq, head_dim, float(scale), 1 if causal else 0, _stream(stream))
 
 
 def row_ops_raw(tiles, n_tiles, row_sum=None, row_max=None, softmax=None, softmax_causal=None,
