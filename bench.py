@@ -263,11 +263,14 @@ def run_ours(args, rank, world, local):
     # directions are independent), as a pipelined host application would run.
     wl2 = Workload(args.workload, rank, world)
     sets = [wl, wl2]
-    host_in = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in w.h2d] for w in sets]
-    host_out = [[torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in w.d2h] for w in sets]
-    for hs, w in zip(host_in, sets):
-        for h, d in zip(hs, w.h2d):
-            h.copy_(d)
+    # One pinned host copy of the inputs and one of the outputs serve both device
+    # sets: copies in one direction are serialised on their stream.
+    host_in_set = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in wl.h2d]
+    host_out_set = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in wl.d2h]
+    for h, d in zip(host_in_set, wl.h2d):
+        h.copy_(d)
+    host_in = [host_in_set, host_in_set]
+    host_out = [host_out_set, host_out_set]
     comp = torch.cuda.current_stream()
     s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
     e2e_steps = max(4, min(args.steps, 8))
@@ -312,7 +315,7 @@ def run_ours(args, rank, world, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
     h2d_bytes = sum(t.numel() * t.element_size() for t in wl.h2d)
     d2h_bytes = sum(t.numel() * t.element_size() for t in wl.d2h)
-    del wl2, host_in, host_out
+    del wl2, host_in, host_out, host_in_set, host_out_set
 
     status = wl.tk.device_status()
     if status != 0:
@@ -378,7 +381,10 @@ def cpu_sample_attention(threads: int, rows_per_thread: int, causal: bool):
     q, k, v = oracle.gen_qkv_normal(4, 1.0, count)  # one (batch, head) slice
 
     def work(i):
-        lo = ATT_S - (i + 1) * rows_per_thread  # late rows: the full key range
+        # Query rows from the end of the sequence (the full key range); threads past
+        # the slice wrap around.
+        lo = (ATT_S - (i + 1) * rows_per_thread) % ATT_S
+        lo = min(lo, ATT_S - rows_per_thread)
         oracle.attention_ref(q, k, v, ATT_S, ATT_D, 1 / math.sqrt(ATT_D), causal, lo, lo + rows_per_thread)
 
     t0 = time.perf_counter()
@@ -393,15 +399,16 @@ def cpu_sample_attention(threads: int, rows_per_thread: int, causal: bool):
     return flops, dt, f"{rows} query rows x 4096 keys x 128 (FP64 attention, P rounded to FP16)"
 
 
-def cpu_baseline(threads: int, workload: str):
-    """Returns (TFLOP/s over the sampled work, description) for the step's mix."""
+def cpu_baseline(threads: int, workload: str, gemm_rows: int = 32, attn_rows: int = 1024):
+    """Returns (TFLOP/s over the sampled work, kind, description, CPU seconds) for the
+    step's FLOP mix. The defaults give about 10 s of CPU work."""
     parts = []
     kind = "port"
     if workload in ("headline", "gemm"):
-        f, dt, kind, desc = cpu_sample_gemm(threads)
+        f, dt, kind, desc = cpu_sample_gemm(threads, rows_per_thread=gemm_rows)
         parts.append((f, dt, desc))
     if workload in ("headline", "attention"):
-        f, dt, desc = cpu_sample_attention(threads, 16, False)
+        f, dt, desc = cpu_sample_attention(threads, min(attn_rows, ATT_S), False)
         parts.append((f, dt, desc))
     if not parts:
         return None
@@ -528,7 +535,8 @@ def main_reference(args):
             val = (n * 1024 * 3 + n * 128) / dt / 1e9
             kind, sample = "port", f"{n} tiles (restated row-tree and FP64 softmax oracles)"
         else:
-            val, kind, sample, dt = cpu_baseline(threads, args.workload)
+            # About 1.5 s of CPU work per step, so the whole run stays within minutes.
+            val, kind, sample, dt = cpu_baseline(threads, args.workload, gemm_rows=4, attn_rows=128)
         if i >= args.warmup:
             values.append(val)
             kinds.add(kind)
