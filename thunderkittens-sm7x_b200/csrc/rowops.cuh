@@ -17,6 +17,7 @@
 #pragma once
 
 #include "tk_ptx.cuh"
+#include "tk_sm7x/tile_b200.cuh"
 
 namespace tk {
 namespace rowops {
@@ -26,26 +27,16 @@ enum : int { kSum = 1, kMax = 2, kSoftmax = 4, kCausal = 8 };
 constexpr int kThreads = 256;            // 8 warps per block
 constexpr int kTilesPerWarpStep = 2;     // tiles in flight per warp step
 
-struct OpSum {
-    __device__ __forceinline__ static float apply(float low, float high) { return low + high; }
-};
-struct OpMax {
-    // include/tk_sm7x/row_reduce_ops.cuh:11-15: ties (and signed zeros) pick high.
-    __device__ __forceinline__ static float apply(float low, float high) {
-        return low > high ? low : high;
-    }
-};
+// The tree, max-tie rule and softmax are the public device-level tile API
+// (include/tk_sm7x/tile_b200.cuh), whose tile16 layout is exactly the layout of a
+// warp's two float4 loads of a tile here.
+using OpSum = tk_sm7x::b200::op_sum;
+using OpMax = tk_sm7x::b200::op_max;
+using tk_sm7x::b200::quad_softmax;
 
-// Full 16-column tree for the row held by this lane's quad (lane & 3 = j).
 template <class Op>
 __device__ __forceinline__ float quad_tree(float x0, float x1, float x2, float x3) {
-    const unsigned j = lane_id() & 3u;
-    float v = Op::apply(Op::apply(x0, x1), Op::apply(x2, x3));
-    float o = __shfl_xor_sync(0xffffffffu, v, 1);
-    v = (j & 1u) ? Op::apply(o, v) : Op::apply(v, o);
-    o = __shfl_xor_sync(0xffffffffu, v, 2);
-    v = (j & 2u) ? Op::apply(o, v) : Op::apply(v, o);
-    return v;
+    return tk_sm7x::b200::quad_reduce<Op>(x0, x1, x2, x3);
 }
 
 template <bool kVec>
@@ -67,42 +58,6 @@ __device__ __forceinline__ void store4(float* p, float4 v) {
         __stcs(p + 2, v.z);
         __stcs(p + 3, v.w);
     }
-}
-
-__device__ __forceinline__ float ex2_approx(float x) {
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// Softmax of the row held by this lane's quad; `row` is the tile row, columns
-// 4j..4j+3 belong to this lane. Causal masks columns > row (include/tk_sm7x/
-// softmax.cuh:69-81): they take no part in the max and sum and their
-// probabilities are written as exactly +0. The max and the sum use the
-// reference's balanced tree. exp(x - m) is computed as 2^((x - m) * log2 e) on the
-// MUFU unit and the normalisation as one correctly rounded reciprocal per row
-// times each exponential: together within ~2e-6 of the FP64 softmax, far inside
-// the 512 * 2^-23 bound of tests/tile_softmax.cu:20, at a few instructions per
-// element instead of a full-precision exponential and an IEEE division.
-template <bool kCausal>
-__device__ __forceinline__ float4 quad_softmax(float4 v, int row) {
-    constexpr float kLog2e = 1.4426950408889634f;
-    const int c0 = static_cast<int>(lane_id() & 3u) * 4;
-    if constexpr (kCausal) {
-        if (c0 + 0 > row) v.x = -INFINITY;
-        if (c0 + 1 > row) v.y = -INFINITY;
-        if (c0 + 2 > row) v.z = -INFINITY;
-        if (c0 + 3 > row) v.w = -INFINITY;
-    }
-    const float m = quad_tree<OpMax>(v.x, v.y, v.z, v.w);
-    float4 e;
-    e.x = ex2_approx((v.x - m) * kLog2e);  // masked: 2^-inf = +0 exactly
-    e.y = ex2_approx((v.y - m) * kLog2e);
-    e.z = ex2_approx((v.z - m) * kLog2e);
-    e.w = ex2_approx((v.w - m) * kLog2e);
-    const float s = quad_tree<OpSum>(e.x, e.y, e.z, e.w);
-    const float inv = __frcp_rn(s);
-    return make_float4(e.x * inv, e.y * inv, e.z * inv, e.w * inv);
 }
 
 template <int kOps, bool kVec>
