@@ -99,6 +99,24 @@ TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowstats_noalloc(int m, int n, int k, 
                                                            float* c, int ldc, float* row_max,
                                                            float* row_sum, cudaStream_t stream);
 
+/* GEMM followed by a full-row softmax of its result, fused: C as
+ * tk_gemm_f16_f16_f32_nn, and P[i][j] = exp(C[i][j] - max_j C[i]) / sum_j exp(...)
+ * over each row's n columns. Generalises the reference's GEMM -> tile softmax
+ * example (examples/gemm_row_softmax.cu:25-48) from one 16x16 tile to full rows. The GEMM
+ * epilogue reduces each 256-column tile of a row to (tile max m_t, sum of
+ * exp(C - m_t)) while the accumulator is still on chip; a second kernel merges the
+ * pairs in tile order and writes P from C (one extra read of C). P is FP32
+ * row-major with leading dimension ldp >= n. P may be C itself (probs == c and
+ * ldp == ldc: C is replaced by P) or lie entirely outside C; A and B must not
+ * overlap C or P. Accuracy: within 512 * 2^-23 of the FP64 softmax of the
+ * returned C per element (the softmax bound of tests/tile_softmax.cu:20).
+ * Scratch for the pairs (m * ceil(n / 256) float pairs) as for the row-statistics
+ * entry point. */
+TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowsoftmax(int m, int n, int k, const void* a,
+                                                     int lda, const void* b, int ldb,
+                                                     float* c, int ldc, float* probs, int ldp,
+                                                     cudaStream_t stream);
+
 /* Tuning knob, no counterpart in the reference (whose tile choice is the fixed
  * rule of src/gemm.cu:50-57): 0 = choose by problem size (default), 1 = one CTA
  * per 128 x 256 tile, 2 = CTA pairs on 256 x 256 tiles. Process-wide; returns

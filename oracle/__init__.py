@@ -69,6 +69,8 @@ def _declare(lib):
         "tko_tile_row_softmax_f64": (None, [_f32p, C.c_size_t, _f64p, C.c_int]),
         "tko_tile_row_softmax_check": (C.c_size_t, [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int,
                                                     C.c_double, C.POINTER(C.c_double)]),
+        "tko_row_softmax_check": (C.c_size_t, [C.c_void_p, C.c_size_t, C.c_size_t, C.c_size_t, C.c_void_p,
+                                               C.c_size_t, C.c_double, C.POINTER(C.c_double)]),
         "tko_attention_ref_f64": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
                                          C.c_double, C.c_int, C.c_int, C.c_int, C.c_void_p,
                                          C.c_void_p]),
@@ -243,6 +245,18 @@ def tile_row_softmax_check(tiles, got, causal: bool, bound: float = SOFTMAX_BOUN
     err = C.c_double()
     fails = lib().tko_tile_row_softmax_check(_ptr(t), _ptr(g), t.size // 256, 1 if causal else 0,
                                              bound, C.byref(err))
+    return int(fails), err.value
+
+
+def row_softmax_check(x, got, bound: float = SOFTMAX_BOUND):
+    """Full-row softmax of the 2-D FP32 array x against `got` (same shape): returns
+    (failures, max_abs_error)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    g = np.ascontiguousarray(got, dtype=np.float32)
+    assert x.shape == g.shape and x.ndim == 2
+    err = C.c_double()
+    fails = lib().tko_row_softmax_check(_ptr(x), x.shape[0], x.shape[1], x.shape[1], _ptr(g), g.shape[1],
+                                        bound, C.byref(err))
     return int(fails), err.value
 
 

@@ -370,4 +370,38 @@ void tko_attention_bound(const uint16_t* v, int s, int d, double* bound_per_col)
     }
 }
 
+// Full-row softmax check: include/tk_sm7x/softmax.cuh:54-64 (exp(x - row max) /
+// row sum) applied to rows of any length n instead of 16 columns, evaluated in
+// FP64 from the FP32 inputs. Each element of `got` must be finite, in [0, 1] and
+// within `bound` of the FP64 value, and each row of `got` must sum to 1 within
+// `bound` (the checks of tests/tile_softmax.cu:160-173, row length generalised).
+size_t tko_row_softmax_check(const float* x, size_t m, size_t n, size_t ldx, const float* got,
+                             size_t ldg, double bound, double* max_err) {
+    size_t failures = 0;
+    double worst = 0.0;
+    std::vector<double> e(n);
+    for (size_t i = 0; i < m; ++i) {
+        const float* row = x + i * ldx;
+        const float* g = got + i * ldg;
+        double maximum = -std::numeric_limits<double>::infinity();
+        for (size_t c = 0; c < n; ++c) maximum = std::fmax(maximum, static_cast<double>(row[c]));
+        double sum = 0.0;
+        for (size_t c = 0; c < n; ++c) {
+            e[c] = std::exp(static_cast<double>(row[c]) - maximum);
+            sum += e[c];
+        }
+        double row_sum = 0.0;
+        for (size_t c = 0; c < n; ++c) {
+            const double want = e[c] / sum;
+            const double err = std::fabs(static_cast<double>(g[c]) - want);
+            if (std::isfinite(err) && err > worst) worst = err;
+            if (!(std::isfinite(g[c]) && g[c] >= 0.0f && g[c] <= 1.0f && err <= bound)) ++failures;
+            row_sum += static_cast<double>(g[c]);
+        }
+        if (!(std::fabs(row_sum - 1.0) <= bound)) ++failures;
+    }
+    if (max_err) *max_err = worst;
+    return failures;
+}
+
 }  // extern "C"

@@ -109,6 +109,10 @@ size_t tko_tile_row_softmax_check(const float* tiles, const float* got,
                                   size_t n_tiles, int causal, double bound,
                                   double* max_err);
 
+/* Softmax over full rows of length n (row pitch ldx / ldg); same checks, FP64. */
+size_t tko_row_softmax_check(const float* x, size_t m, size_t n, size_t ldx, const float* got,
+                             size_t ldg, double bound, double* max_err);
+
 /* ---- attention ------------------------------------------------------------- */
 /* One (batch, head) slice: q, k, v are s x d row-major binary16. For query rows
  * [row_begin, row_end): FP64 scores * scale, max over allowed keys, exp,

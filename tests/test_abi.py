@@ -68,6 +68,29 @@ def test_gemm_invalid_arguments(over):
     assert code == INVALID
 
 
+@pytest.mark.parametrize("over", [
+    dict(a=None), dict(b=None), dict(c=None), dict(m=0), dict(n=17), dict(k=-16), dict(lda=15),
+    dict(ldb=15), dict(ldc=15),
+], ids=lambda d: ",".join(f"{k}={v}" for k, v in d.items()))
+def test_gemm_rowsoftmax_invalid_arguments(over):
+    a = gemm_args(**over)
+    code = tk_b200.lib().tk_gemm_f16_f16_f32_nn_rowsoftmax(a["m"], a["n"], a["k"], a["a"], a["lda"], a["b"],
+                                                            a["ldb"], a["c"], a["ldc"], FAKE * 8, 16, None)
+    assert code == INVALID
+
+
+def test_gemm_rowsoftmax_output_rules():
+    lib = tk_b200.lib()
+    a = gemm_args(m=32)
+    call = lambda probs, ldp, ldc=16: lib.tk_gemm_f16_f16_f32_nn_rowsoftmax(  # noqa: E731
+        32, 16, 16, a["a"], 16, a["b"], 16, a["c"], ldc, probs, ldp, None)
+    assert call(None, 16) == INVALID            # no output
+    assert call(FAKE * 8, 15) == INVALID        # ldp < n
+    assert call(a["c"] + 64, 16) == INVALID     # partial overlap of P and C
+    assert call(a["c"], 32) == INVALID          # same base, different pitch
+    assert call(a["c"] - 4 * 16 * 32 + 4, 16) == INVALID  # P's last row reaches C
+
+
 def test_gemm_rowstats_needs_both_outputs():
     a = gemm_args()
     lib = tk_b200.lib()

@@ -183,6 +183,24 @@ def test_softmax_check_detects_planted_error():
     assert oracle.tile_row_softmax_check(logits, causal, True)[0] > 0
 
 
+def test_row_softmax_check_agrees_with_tile_softmax_and_detects_errors():
+    """The full-row checker on 16-column rows is the tile checker; planted errors
+    (one element off, a row that no longer sums to 1) are rejected."""
+    logits = fx.softmax_logits(3, 0)
+    want = oracle.tile_row_softmax_f64(logits, False).astype(np.float32)
+    assert oracle.row_softmax_check(logits.reshape(-1, 16), want.reshape(-1, 16))[0] == 0
+    x = oracle.gen_normal_f32(8, 4.0, 6 * 1000).reshape(6, 1000)
+    e = np.exp(x.astype(np.float64) - x.max(axis=1, keepdims=True))
+    good = (e / e.sum(axis=1, keepdims=True)).astype(np.float32)
+    assert oracle.row_softmax_check(x, good)[0] == 0
+    bad = good.copy()
+    bad[4, 17] += np.float32(2e-4)
+    assert oracle.row_softmax_check(x, bad)[0] > 0
+    scaled = good * np.float32(1.0 + 2e-4)  # every element within bound, the row sum not
+    fails, _ = oracle.row_softmax_check(x, scaled)
+    assert fails > 0
+
+
 def test_pairwise_reduce_matches_tree():
     x = oracle.gen_normal_f32(5, 2.0, 16)
     assert oracle.pairwise_reduce(x, "sum") == oracle.lib().tko_row_tree16(x, 0)

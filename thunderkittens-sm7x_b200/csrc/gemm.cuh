@@ -25,6 +25,7 @@
 #pragma once
 
 #include "tk_ptx.cuh"
+#include "tk_sm7x/tile_b200.cuh"
 
 namespace tk {
 namespace gemm {
@@ -84,22 +85,9 @@ __device__ __forceinline__ void work_coords(int t, const Params& p, int* tm, int
     *kb1 = min(*kb0 + p.kb_per_split, p.k_blocks);
 }
 
-struct OpSumG {
-    __device__ __forceinline__ static float apply(float lo, float hi) { return lo + hi; }
-};
-struct OpMaxG {
-    __device__ __forceinline__ static float apply(float lo, float hi) { return lo > hi ? lo : hi; }
-};
-
-// Canonical balanced tree over 16 consecutive values.
-template <class Op>
-__device__ __forceinline__ float tree16(const float* x) {
-    const float q0 = Op::apply(Op::apply(x[0], x[1]), Op::apply(x[2], x[3]));
-    const float q1 = Op::apply(Op::apply(x[4], x[5]), Op::apply(x[6], x[7]));
-    const float q2 = Op::apply(Op::apply(x[8], x[9]), Op::apply(x[10], x[11]));
-    const float q3 = Op::apply(Op::apply(x[12], x[13]), Op::apply(x[14], x[15]));
-    return Op::apply(Op::apply(q0, q1), Op::apply(q2, q3));
-}
+using OpSumG = tk_sm7x::b200::op_sum;
+using OpMaxG = tk_sm7x::b200::op_max;
+using tk_sm7x::b200::tree16;  // canonical balanced tree over 16 consecutive values
 
 // Level-by-level pairwise reduction of g[0..count) (count <= 16), odd last
 // element carried up; fully unrolled so g stays in registers.
@@ -118,7 +106,14 @@ __device__ __forceinline__ float pairwise16(float (&g)[16], int count) {
     return g[0];
 }
 
-template <int kCtaGroup, bool kRowStats>
+// Epilogue statistics per (row, 256-column tile), written to Params::partial:
+enum Stats : int {
+    kStatsNone = 0,
+    kStatsMaxSum = 1,   // (row max, row sum) of the tile's columns, fixed pairwise order
+    kStatsSoftmax = 2,  // (row max m_t, sum of exp(c - m_t)) for a full-row softmax
+};
+
+template <int kCtaGroup, int kStats>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const Params p) {
@@ -326,15 +321,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (col0 + q < p.n) crow[col0 + q] = __uint_as_float(r[q]);
                     }
                 }
-                if constexpr (kRowStats) {
+                if constexpr (kStats != kStatsNone) {
                     float x[32];
 #pragma unroll
                     for (int q = 0; q < 32; ++q) x[q] = __uint_as_float(r[q]);
                     gmax[2 * chunk] = tree16<OpMaxG>(x);
                     gmax[2 * chunk + 1] = tree16<OpMaxG>(x + 16);
-                    gsum[2 * chunk] = tree16<OpSumG>(x);
-                    gsum[2 * chunk + 1] = tree16<OpSumG>(x + 16);
+                    if constexpr (kStats == kStatsMaxSum) {
+                        gsum[2 * chunk] = tree16<OpSumG>(x);
+                        gsum[2 * chunk + 1] = tree16<OpSumG>(x + 16);
+                    }
                 }
+            }
+            if constexpr (kStats == kStatsSoftmax) {
+                // Second read of the accumulator: sum of exp(c - m_t) over this
+                // tile's valid columns, m_t the tile-row max (warp-uniform loop).
+                const int groups = max(0, min(16, (p.n - col_base) / 16));
+                const float m_t = pairwise16<OpMaxG>(gmax, groups);
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int chunk = 0; chunk < kBlockN / 32; ++chunk) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_addr + chunk * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int q = 0; q < 32; ++q) {
+                        if (col_base + chunk * 32 + q < p.n)
+                            acc[q & 3] += tk_sm7x::b200::ex2_approx(
+                                (__uint_as_float(r[q]) - m_t) * 1.4426950408889634f);
+                    }
+                }
+                gmax[0] = m_t;
+                gsum[0] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
             }
             tc_fence_before();
             __syncwarp();
@@ -345,13 +363,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_cluster(tempty_remote + 8u * acc);
                 }
             }
-            if constexpr (kRowStats) {
+            if constexpr (kStats == kStatsMaxSum) {
                 if (row_ok) {
                     const int groups = min(16, (p.n - col_base) / 16);
                     const float mx = pairwise16<OpMaxG>(gmax, groups);
                     const float sm = pairwise16<OpSumG>(gsum, groups);
                     float2* dst = reinterpret_cast<float2*>(p.partial) + (row * p.n_tiles + tn);
                     *dst = make_float2(mx, sm);
+                }
+            }
+            if constexpr (kStats == kStatsSoftmax) {
+                if (row_ok) {
+                    float2* dst = reinterpret_cast<float2*>(p.partial) + (row * p.n_tiles + tn);
+                    *dst = make_float2(gmax[0], gsum[0]);
                 }
             }
             if (++acc == 2) {
@@ -404,6 +428,49 @@ __global__ void rowstats_finish_kernel(const float2* partial, int m, int n_tiles
     }
     row_max[row] = vmax;
     row_sum[row] = vsum;
+}
+
+// Full-row softmax from the per-tile (m_t, sum exp(c - m_t)) pairs, one warp per
+// row: the lanes merge the pairs (row max M, normaliser S = sum s_t exp(m_t - M),
+// a fixed shuffle order, so the result is deterministic), then the warp writes
+// p = exp(c - M) / S over the row. p may be c itself: each element is read before
+// the same lane overwrites it.
+__global__ void __launch_bounds__(256) rowsoftmax_apply_kernel(const float2* partial, int m, int n,
+                                                               int n_tiles, const float* c, long long ldc,
+                                                               float* p, long long ldp, bool vec4) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+    for (long long row = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); row < m;
+         row += warps) {
+        const float2* src = partial + row * n_tiles;
+        float big = -INFINITY;
+        for (int t = lane; t < n_tiles; t += 32) big = fmaxf(big, src[t].x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) big = fmaxf(big, __shfl_xor_sync(0xffffffffu, big, o));
+        float total = 0.0f;
+        for (int t = lane; t < n_tiles; t += 32)
+            total += src[t].y * tk_sm7x::b200::ex2_approx((src[t].x - big) * kLog2e);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+        const float inv = __frcp_rn(total);
+        const float* crow = c + row * ldc;
+        float* prow = p + row * ldp;
+        if (vec4) {
+            for (int j = lane * 4; j < n; j += 128) {
+                const float4 v = __ldcs(reinterpret_cast<const float4*>(crow + j));
+                float4 o;
+                o.x = tk_sm7x::b200::ex2_approx((v.x - big) * kLog2e) * inv;
+                o.y = tk_sm7x::b200::ex2_approx((v.y - big) * kLog2e) * inv;
+                o.z = tk_sm7x::b200::ex2_approx((v.z - big) * kLog2e) * inv;
+                o.w = tk_sm7x::b200::ex2_approx((v.w - big) * kLog2e) * inv;
+                __stcs(reinterpret_cast<float4*>(prow + j), o);
+            }
+        } else {
+            for (int j = lane; j < n; j += 32)
+                prow[j] = tk_sm7x::b200::ex2_approx((crow[j] - big) * kLog2e) * inv;
+        }
+    }
 }
 
 // Sums the split-K partials ws[0..splits)[m][n] in split order into C (ldc).

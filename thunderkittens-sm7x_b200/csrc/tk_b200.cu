@@ -115,11 +115,11 @@ cudaError_t rowops(const float* tiles, size_t n_tiles, float* sum_out, float* ma
 
 int g_gemm_cta_group_override = 0;  // 0 = choose by problem size
 
-template <int kCtaGroup, bool kRowStats>
+template <int kCtaGroup, int kStats>
 cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
                                int device, int sm_count, cudaStream_t stream) {
     using Cfg = tk::gemm::Cfg<kCtaGroup>;
-    auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kRowStats>;
+    auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kStats>;
     static bool configured[tk::host::kMaxDevices] = {};
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -145,14 +145,24 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
 }
 
 cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b, int ldb, float* c,
-                      int ldc, float* row_max, float* row_sum, cudaStream_t stream) {
-    const bool stats = row_max != nullptr || row_sum != nullptr;
+                      int ldc, float* row_max, float* row_sum, float* probs, int ldp, cudaStream_t stream) {
+    const bool softmax = probs != nullptr;
+    const bool stats = row_max != nullptr || row_sum != nullptr || softmax;
     if (a == nullptr || b == nullptr || c == nullptr || m <= 0 || n <= 0 || k <= 0 || m % 16 != 0 ||
         n % 16 != 0 || k % 16 != 0 || lda < k || ldb < n || ldc < n) {
         return cudaErrorInvalidValue;
     }
-    if (stats && (row_max == nullptr || row_sum == nullptr ||
-                  tk::host::ranges_overlap(row_max, sizeof(float) * m, row_sum, sizeof(float) * m))) {
+    if (softmax) {
+        if (ldp < n) return cudaErrorInvalidValue;
+        // P either replaces C exactly (in place) or lies entirely outside it.
+        const size_t c_bytes = (static_cast<size_t>(m - 1) * ldc + n) * sizeof(float);
+        const size_t p_bytes = (static_cast<size_t>(m - 1) * ldp + n) * sizeof(float);
+        if (!(probs == c && ldp == ldc) && tk::host::ranges_overlap(probs, p_bytes, c, c_bytes))
+            return cudaErrorInvalidValue;
+    }
+    if (stats && !softmax &&
+        (row_max == nullptr || row_sum == nullptr ||
+         tk::host::ranges_overlap(row_max, sizeof(float) * m, row_sum, sizeof(float) * m))) {
         return cudaErrorInvalidValue;
     }
     int sm_count = 0, device = 0;
@@ -262,14 +272,25 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     }
     p.partial = partial;
 
+    using tk::gemm::kStatsMaxSum;
+    using tk::gemm::kStatsNone;
+    using tk::gemm::kStatsSoftmax;
     if (cta_group == 2) {
-        err = stats ? launch_gemm_kernel<2, true>(ma, mb, p, device, sm_count, stream)
-                    : launch_gemm_kernel<2, false>(ma, mb, p, device, sm_count, stream);
+        err = softmax ? launch_gemm_kernel<2, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
+              : stats ? launch_gemm_kernel<2, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
+                      : launch_gemm_kernel<2, kStatsNone>(ma, mb, p, device, sm_count, stream);
     } else {
-        err = stats ? launch_gemm_kernel<1, true>(ma, mb, p, device, sm_count, stream)
-                    : launch_gemm_kernel<1, false>(ma, mb, p, device, sm_count, stream);
+        err = softmax ? launch_gemm_kernel<1, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
+              : stats ? launch_gemm_kernel<1, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
+                      : launch_gemm_kernel<1, kStatsNone>(ma, mb, p, device, sm_count, stream);
     }
-    if (stats && err == cudaSuccess) {
+    if (softmax && err == cudaSuccess) {
+        const bool vec4 = aligned(c, 16) && ldc % 4 == 0 && aligned(probs, 16) && ldp % 4 == 0;
+        const int warps_needed = (m + 7) / 8;  // 8 rows (warps) per block
+        const int blocks = warps_needed < 8 * sm_count ? warps_needed : 8 * sm_count;
+        tk::gemm::rowsoftmax_apply_kernel<<<blocks, 256, 0, stream>>>(
+            reinterpret_cast<const float2*>(partial), m, n, p.n_tiles, c, ldc, probs, ldp, vec4);
+    } else if (stats && err == cudaSuccess) {
         tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(
             reinterpret_cast<const float2*>(partial), m, p.n_tiles, row_max, row_sum);
     }
@@ -370,8 +391,8 @@ cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, c
     // Every (row < m, tile) pair is written by the GEMM epilogue before the
     // finishing pass reads it, so nothing left by an earlier call is ever used.
     p.partial = reinterpret_cast<float*>(scratch);
-    err = cta_group == 2 ? launch_gemm_kernel<2, true>(ma, mb, p, device, sm_count, stream)
-                         : launch_gemm_kernel<1, true>(ma, mb, p, device, sm_count, stream);
+    err = cta_group == 2 ? launch_gemm_kernel<2, tk::gemm::kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
+                         : launch_gemm_kernel<1, tk::gemm::kStatsMaxSum>(ma, mb, p, device, sm_count, stream);
     if (err != cudaSuccess) return err;
     tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(scratch, m, p.n_tiles, row_max,
                                                                          row_sum);
@@ -384,14 +405,14 @@ extern "C" {
 
 cudaError_t tk_gemm_f16_f16_f32_nn(int m, int n, int k, const void* a, int lda, const void* b,
                                    int ldb, float* c, int ldc, cudaStream_t stream) {
-    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, nullptr, nullptr, stream);
+    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, nullptr, nullptr, nullptr, 0, stream);
 }
 
 cudaError_t tk_gemm_f16_f16_f32_nn_rowstats(int m, int n, int k, const void* a, int lda,
                                             const void* b, int ldb, float* c, int ldc,
                                             float* row_max, float* row_sum, cudaStream_t stream) {
     if (row_max == nullptr || row_sum == nullptr) return cudaErrorInvalidValue;
-    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream);
+    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, nullptr, 0, stream);
 }
 
 cudaError_t tk_gemm_f16_f16_f32_nn_rowstats_noalloc(int m, int n, int k, const void* a, int lda,
@@ -399,6 +420,13 @@ cudaError_t tk_gemm_f16_f16_f32_nn_rowstats_noalloc(int m, int n, int k, const v
                                                     float* row_max, float* row_sum,
                                                     cudaStream_t stream) {
     return gemm_rowstats_noalloc(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream);
+}
+
+cudaError_t tk_gemm_f16_f16_f32_nn_rowsoftmax(int m, int n, int k, const void* a, int lda,
+                                              const void* b, int ldb, float* c, int ldc, float* probs,
+                                              int ldp, cudaStream_t stream) {
+    if (probs == nullptr) return cudaErrorInvalidValue;
+    return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, nullptr, nullptr, probs, ldp, stream);
 }
 
 int tk_gemm_set_cta_group(int cta_group) {

@@ -33,6 +33,7 @@ SIGNATURES = {
     "tk_gemm_f16_f16_f32_nn_rowstats": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _VP, _VP]),
     "tk_gemm_f16_f16_f32_nn_rowstats_noalloc": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _VP,
                                                      _VP]),
+    "tk_gemm_f16_f16_f32_nn_rowsoftmax": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _I, _VP]),
     "tk_gemm_set_cta_group": (_I, [_I]),
     "tk_tile_row_sum_f32": (_I, [_VP, _SZ, _VP, _VP]),
     "tk_tile_row_max_f32": (_I, [_VP, _SZ, _VP, _VP]),
@@ -109,6 +110,11 @@ def gemm_rowstats_raw(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream=
                                                  _ptr(row_max), _ptr(row_sum), _stream(stream))
 
 
+def gemm_rowsoftmax_raw(m, n, k, a, lda, b, ldb, c, ldc, probs, ldp, stream=None) -> int:
+    return lib().tk_gemm_f16_f16_f32_nn_rowsoftmax(m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c), ldc,
+                                                   _ptr(probs), ldp, _stream(stream))
+
+
 def set_gemm_cta_group(g: int) -> int:
     return lib().tk_gemm_set_cta_group(g)
 
@@ -168,6 +174,23 @@ def gemm_rowstats(a, b, c=None, *, stream=None):
            gemm_rowstats_raw(m, n, k, a, a.stride(0), b, b.stride(0), c, c.stride(0), row_max, row_sum,
                              stream))
     return c, row_max, row_sum
+
+
+def gemm_rowsoftmax(a, b, c=None, probs=None, *, in_place=False, stream=None):
+    """C = A @ B and P = softmax over each row of C. With in_place=True P replaces C
+    (one buffer); returns (C, P), the same tensor twice when in place."""
+    import torch
+    m, n, k = a.shape[0], b.shape[1], b.shape[0]
+    if c is None:
+        c = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    if in_place:
+        probs = c
+    elif probs is None:
+        probs = torch.empty((m, n), dtype=torch.float32, device=a.device)
+    _check("tk_gemm_f16_f16_f32_nn_rowsoftmax",
+           gemm_rowsoftmax_raw(m, n, k, a, a.stride(0), b, b.stride(0), c, c.stride(0), probs,
+                               probs.stride(0), stream))
+    return c, probs
 
 
 def tile_row_ops(tiles, *, ops=("sum", "max", "softmax", "causal"), stream=None):
