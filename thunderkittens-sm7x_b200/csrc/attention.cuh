@@ -44,13 +44,14 @@ constexpr int kBlockQ = 128;
 constexpr int kBlockKV = 128;
 constexpr int kKvSlots = 4;
 constexpr uint32_t kTmemCols = 512;
-// One score in kFmaExpEvery takes the FMA-pipe exponential (the rest use MUFU);
-// 0 sends every score to MUFU. Measured on B200 at [8,32,4096,128]: every 4 / 8 /
-// 16 / none gave 973 / 1032 / 1008 / 1040 TFLOP/s, so MUFU alone is the default.
-#ifndef TK_ATTN_FMA_EXP_EVERY
-#define TK_ATTN_FMA_EXP_EVERY 0
+// In the unmasked fast path, one score pair in kPolyPairEvery takes exp2_poly2 on
+// the FMA pipe instead of two MUFU exponentials (0: none). Measured on B200 at
+// [8,32,4096,128]: every 4th / 3rd / 2nd pair gave 1061 / 1047 / 979 TFLOP/s
+// against 1124 with MUFU alone, so the default is none.
+#ifndef TK_ATTN_POLY_PAIR_EVERY
+#define TK_ATTN_POLY_PAIR_EVERY 0
 #endif
-constexpr int kFmaExpEvery = TK_ATTN_FMA_EXP_EVERY;
+constexpr int kPolyPairEvery = TK_ATTN_POLY_PAIR_EVERY;
 
 template <int kDPad>
 struct Cfg {
@@ -84,26 +85,48 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// 2^x on the FMA pipe, available to move a share of the exponentials off the MUFU
-// unit (kFmaExpEvery). Cody-Waite split x = n + f with n = rint(x), f in [-0.5, 0.5];
-// 2^f from a degree-5 polynomial (least-squares fit on Chebyshev nodes of
-// [-0.5, 0.5], constant term pinned to 1; max relative error 1.8e-7, i.e. within
-// ~1.5 ulp of FP32); 2^n applied by adding n to the exponent field. Inputs are
-// clamped at -125 so the result stays a normal float; anything that small rounds
-// to 0 in binary16.
-__device__ __forceinline__ float exp2_fma(float x) {
-    x = fmaxf(x, -125.0f);
-    const float shifter = 12582912.0f;  // 1.5 * 2^23: x + shifter holds rint(x) in its low bits
-    const float t = x + shifter;
-    const float n = t - shifter;
-    const float f = x - n;
-    float p = 1.3218672e-3f;
-    p = fmaf(p, f, 9.6716983e-3f);
-    p = fmaf(p, f, 5.5508930e-2f);
-    p = fmaf(p, f, 2.4022238e-1f);
-    p = fmaf(p, f, 6.9314688e-1f);
-    p = fmaf(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed FP32 pairs (sm_100 f32x2 arithmetic: two lanes of work per instruction).
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\tmov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+        "mov.b64 rc, {%5, %6};\n\tfma.rn.f32x2 %0, ra, rb, rc;\n\t}"
+        : "=l"(d)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+    return r;
+}
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    uint64_t d;
+    asm("{\n\t.reg .b64 ra, rb;\n\tmov.b64 ra, {%1, %2};\n\tmov.b64 rb, {%3, %4};\n\t"
+        "add.rn.f32x2 %0, ra, rb;\n\t}"
+        : "=l"(d)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+    return r;
+}
+
+// 2^x for a pair on the FMA pipe (packed FP32 arithmetic), to move a share of the
+// exponentials off the MUFU unit. x = n + f with n = rint(x) (the 1.5 * 2^23
+// shifter leaves n in the low bits of t), f in [-0.5, 0.5]; 2^f from a degree-4
+// polynomial with constant term 1 (least-squares fit on Chebyshev nodes, then
+// reweighted towards equal ripple; max relative error 2.9e-6, far below binary16's
+// half ulp 2^-11); 2^n is added to the exponent field. Inputs are clamped at -125
+// so the result stays a normal float; anything that small rounds to 0 in binary16.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    x.x = fmaxf(x.x, -125.0f);
+    x.y = fmaxf(x.y, -125.0f);
+    const float2 t = add2(x, make_float2(12582912.0f, 12582912.0f));
+    const float2 n = add2(t, make_float2(-12582912.0f, -12582912.0f));
+    const float2 f = fma2(n, make_float2(-1.0f, -1.0f), x);
+    float2 q = fma2(make_float2(9.58281010e-3f, 9.58281010e-3f), f, make_float2(5.59064224e-2f, 5.59064224e-2f));
+    q = fma2(q, f, make_float2(2.40240991e-1f, 2.40240991e-1f));
+    q = fma2(q, f, make_float2(6.93124175e-1f, 6.93124175e-1f));
+    q = fma2(q, f, make_float2(1.0f, 1.0f));
+    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -144,8 +167,8 @@ __device__ __forceinline__ float score_row_max(uint32_t s_addr, int limit, bool 
 }
 
 // Exponentials 2^(s * c_eff - m) of the row, chunk by chunk, with the next chunk's
-// TMEM load in flight while the current one is computed. One score in eight goes
-// to the FMA pipe (exp2_fma), the rest to MUFU. kMode 0: write binary16 P (over
+// TMEM load in flight while the current one is computed (masked blocks and the
+// single-block path; unmasked blocks take row_exp_store128). kMode 0: write binary16 P (over
 // the S columns already consumed) and return the sum; 1: only return the sum;
 // 2: write binary16 P / norm (exact normalise-then-round of a single key block).
 template <bool kFast, int kMode>
@@ -164,10 +187,7 @@ __device__ __forceinline__ float score_row_exp(uint32_t s_addr, int limit, bool 
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             const float v = kFast ? __uint_as_float(r[c & 1][i]) : score_slow(r[c & 1][i], 32 * c + i, limit, pos_scale, c_in);
-            const float arg = fmaf(v, c_eff, neg_m);
-            e[i] = (kFmaExpEvery > 0 && i % (kFmaExpEvery > 0 ? kFmaExpEvery : 1) == kFmaExpEvery - 1)
-                       ? exp2_fma(arg)
-                       : ex2(arg);
+            e[i] = ex2(fmaf(v, c_eff, neg_m));
             acc[i & 7] += e[i];
         }
         if constexpr (kMode != 1) {
@@ -185,6 +205,69 @@ __device__ __forceinline__ float score_row_exp(uint32_t s_addr, int limit, bool 
         if (c < 3) tmem_wait_ld();
     }
     return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
+}
+
+// Fast path of a block with no masked key and a positive scale: the thread's
+// whole 128-score row comes into registers with one TMEM round trip (four loads
+// in flight, one wait); the max, the exponentials, their sum and the binary16 P
+// are then computed from registers.
+__device__ __forceinline__ void load_row128(uint32_t s_addr, uint32_t (&r)[128]) {
+    tmem_ld_32x32b_x32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    tmem_ld_32x32b_x32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+    tmem_ld_32x32b_x32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
+    tmem_ld_32x32b_x32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
+    tmem_wait_ld();
+}
+
+__device__ __forceinline__ float row_max128(const uint32_t (&r)[128]) {
+    float mx[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) mx[t] = __uint_as_float(r[t]);
+#pragma unroll
+    for (int i = 8; i < 128; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
+    return fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+}
+
+// 2^(s * c - m) for the 128 scores; writes binary16 P over the first 64 columns
+// (whose scores are already in registers) and returns the sum. The exponent
+// arguments and the running sums use packed FP32 pairs.
+__device__ __forceinline__ float row_exp_store128(uint32_t s_addr, const uint32_t (&r)[128], float c,
+                                                  float neg_m) {
+    float2 acc[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) acc[t] = make_float2(0.0f, 0.0f);
+    const float2 c2 = make_float2(c, c);
+    const float2 m2 = make_float2(neg_m, neg_m);
+#pragma unroll
+    for (int chunk = 0; chunk < 4; ++chunk) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int idx = 32 * chunk + 2 * i;
+            const float2 a = fma2(make_float2(__uint_as_float(r[idx]), __uint_as_float(r[idx + 1])), c2, m2);
+            const bool poly = kPolyPairEvery > 0 && i % (kPolyPairEvery > 0 ? kPolyPairEvery : 1) == kPolyPairEvery - 1;
+            const float2 e = poly ? exp2_poly2(a) : make_float2(ex2(a.x), ex2(a.y));
+            acc[i & 3] = add2(acc[i & 3], e);
+            pk[i] = pack_half2(e.x, e.y);
+        }
+        tmem_st_32x32b_x16(s_addr + 16 * chunk, pk);
+    }
+    const float2 s01 = add2(acc[0], acc[1]);
+    const float2 s23 = add2(acc[2], acc[3]);
+    const float2 t = add2(s01, s23);
+    return t.x + t.y;
+}
+
+// Moves the running reference point m_run (log2 units) for a block whose max is
+// m_blk. The point only moves when the max grows by more than 8 (so unnormalised
+// probabilities stay <= 2^8); otherwise O needs no rescale. The first block always
+// sets it, so a single-block row uses its exact max. A row with no allowed key yet
+// (only padding rows) keeps a finite point. alpha rescales O and the running sum.
+__device__ __forceinline__ void next_point(float m_run, float m_blk, float& m_use, float& alpha) {
+    const float m_new = fmaxf(m_run, m_blk);
+    m_use = m_new > m_run + 8.0f ? m_new : m_run;
+    if (m_use == -INFINITY) m_use = 0.0f;
+    alpha = m_use == m_run ? 1.0f : ex2(m_run - m_use);
 }
 
 template <int kDPad>
@@ -294,99 +377,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 9) {
-        // ---------------- MMA issuer ----------------
-        bool ok = mbar_wait_warp(q_full, 0, kFaultAttnWait, abort_flag);
-        tc_fence_after();
-        const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
-        uint32_t pr_phase[2] = {0, 0};
-        int prev_v_slot = 0;
-        for (int j = 0; j < n_blocks && ok; ++j) {
-            const int k_slot = (2 * j) % kKvSlots;
-            const int v_slot = (2 * j + 1) % kKvSlots;
-            const uint32_t k_phase = static_cast<uint32_t>((2 * j) / kKvSlots) & 1u;
-            const uint32_t v_phase = static_cast<uint32_t>((2 * j + 1) / kKvSlots) & 1u;
-            if (!mbar_wait_warp(kv_full(k_slot), k_phase, kFaultAttnWait, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t k_addr = base + C::kKvOffset + k_slot * C::kTileBytes;
-            const uint32_t v_addr = base + C::kKvOffset + v_slot * C::kTileBytes;
-            // S0_j = Q0 K_j^T
-            if (lane == 0) {
+        // ---------------- MMA issuer (one thread) ----------------
+        // Issue order per key block j: S0_j, PV1_{j-1}, S1_j, PV0_j. Before PV0_j the
+        // thread also waits for K_{j+1}, so PV0_j and S0_{j+1} go to the tensor pipe
+        // back to back: the chain PV0_j -> S0_{j+1} -> softmax 0 is the critical path.
+        if (lane == 0) {
+            const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
+            auto kv_addr = [&](int slot) { return base + C::kKvOffset + slot * C::kTileBytes; };
+            auto kv_phase = [&](int load) { return static_cast<uint32_t>(load / kKvSlots) & 1u; };
+            auto issue_s = [&](int g, uint32_t k_addr) {
 #pragma unroll
                 for (int kk = 0; kk < kDPad / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    mma_f16_ss<1>(tmem + 0, sw128_desc(q_addr[0] + off, 16, 1024),
+                    mma_f16_ss<1>(tmem + 256u * g, sw128_desc(q_addr[g] + off, 16, 1024),
                                   sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
                 }
-                mma_commit(s_full(0));
-            }
-            __syncwarp();
-            // PV1_{j-1}
-            if (j > 0 && has_tile1) {
-                if (!mbar_wait_warp(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                pr_phase[1] ^= 1u;
-                tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t pv_addr = base + C::kKvOffset + prev_v_slot * C::kTileBytes;
-#pragma unroll
-                    for (int kk = 0; kk < kBlockKV / 16; ++kk)
-                        mma_f16_ts(tmem + 256 + 128, tmem + 256 + kk * 8,
-                                   sw128_desc(pv_addr + kk * 2048, 16384, 1024), C::kIdescO,
-                                   (j - 1 > 0 || kk > 0) ? 1u : 0u);
-                }
-                __syncwarp();
-            }
-            if (j > 0 && lane == 0) mma_commit(kv_empty(prev_v_slot));
-            __syncwarp();
-            // S1_j = Q1 K_j^T
-            if (has_tile1) {
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < kDPad / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        mma_f16_ss<1>(tmem + 256, sw128_desc(q_addr[1] + off, 16, 1024),
-                                      sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
-                    }
-                    mma_commit(s_full(1));
-                }
-                __syncwarp();
-            }
-            if (lane == 0) mma_commit(kv_empty(k_slot));
-            __syncwarp();
-            // PV0_j
-            if (!mbar_wait_warp(kv_full(v_slot), v_phase, kFaultAttnWait, abort_flag)) break;
-            if (!mbar_wait_warp(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
-            pr_phase[0] ^= 1u;
-            tc_fence_after();
-            if (lane == 0) {
+                mma_commit(s_full(g));
+            };
+            auto issue_pv = [&](int g, uint32_t v_addr, bool first) {
 #pragma unroll
                 for (int kk = 0; kk < kBlockKV / 16; ++kk)
-                    mma_f16_ts(tmem + 128, tmem + kk * 8, sw128_desc(v_addr + kk * 2048, 16384, 1024),
-                               C::kIdescO, (j > 0 || kk > 0) ? 1u : 0u);
-                if (j == n_blocks - 1) mma_commit(o_final(0));
-            }
-            __syncwarp();
-            prev_v_slot = v_slot;
-            if (j == n_blocks - 1) {
-                // PV1_last
-                if (has_tile1) {
-                    if (!mbar_wait_warp(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                    pr_phase[1] ^= 1u;
-                    tc_fence_after();
-                    if (lane == 0) {
-#pragma unroll
-                        for (int kk = 0; kk < kBlockKV / 16; ++kk)
-                            mma_f16_ts(tmem + 256 + 128, tmem + 256 + kk * 8,
-                                       sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
-                                       (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + 256u * g + 128u, tmem + 256u * g + kk * 8,
+                               sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
+                               (!first || kk > 0) ? 1u : 0u);
+            };
+            uint32_t pr_phase[2] = {0, 0};
+            bool ok = mbar_wait(q_full, 0, kFaultAttnWait, abort_flag) &&
+                      mbar_wait(kv_full(0), 0, kFaultAttnWait, abort_flag);
+            tc_fence_after();
+            if (ok) issue_s(0, kv_addr(0));
+            for (int j = 0; j < n_blocks && ok; ++j) {
+                const int k_slot = (2 * j) % kKvSlots;
+                const int v_slot = (2 * j + 1) % kKvSlots;
+                const int prev_v_slot = (2 * j - 1 + kKvSlots) % kKvSlots;
+                const bool last = j == n_blocks - 1;
+                // PV1_{j-1}, then V_{j-1} is free
+                if (j > 0) {
+                    if (has_tile1) {
+                        if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                        pr_phase[1] ^= 1u;
+                        tc_fence_after();
+                        issue_pv(1, kv_addr(prev_v_slot), j == 1);
+                    }
+                    mma_commit(kv_empty(prev_v_slot));
+                }
+                // S1_j, then K_j is free
+                if (has_tile1) issue_s(1, kv_addr(k_slot));
+                mma_commit(kv_empty(k_slot));
+                // PV0_j and S0_{j+1}, back to back
+                if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
+                const int next_k_slot = (2 * j + 2) % kKvSlots;
+                if (!last && !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
+                    break;
+                if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
+                pr_phase[0] ^= 1u;
+                tc_fence_after();
+                issue_pv(0, kv_addr(v_slot), j == 0);
+                if (last) {
+                    mma_commit(o_final(0));
+                } else {
+                    issue_s(0, kv_addr(next_k_slot));
+                }
+                if (last) {
+                    // PV1_last
+                    if (has_tile1) {
+                        if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                        pr_phase[1] ^= 1u;
+                        tc_fence_after();
+                        issue_pv(1, kv_addr(v_slot), j == 0);
                         mma_commit(o_final(1));
                     }
-                    __syncwarp();
+                    mma_commit(kv_empty(v_slot));
                 }
-                if (lane == 0) mma_commit(kv_empty(v_slot));
-                __syncwarp();
             }
         }
-    } else {
+        __syncwarp();
+    } else if (warp < 8) {
         // ---------------- softmax warpgroups (warps 0-3: tile 0, 4-7: tile 1) ----------------
         const int g = static_cast<int>(warp >> 2);
         const uint32_t quarter = warp & 3u;
@@ -418,32 +484,30 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool pos_scale = c_in > 0.0f;
             const float c_eff = pos_scale ? c_in : 1.0f;
             const bool fast = pos_scale && !need_mask;
-            const float m_raw = fast ? score_row_max<true>(s_addr, limit, pos_scale, c_in)
-                                     : score_row_max<false>(s_addr, limit, pos_scale, c_in);
-            const float m_blk = m_raw * c_eff;
-            const float m_new = fmaxf(m_run, m_blk);
-            // The reference point only moves when the max grows by more than 8 (so
-            // unnormalised probabilities stay <= 2^8); otherwise O needs no rescale.
-            // The first block always sets it, so a single-block row uses its exact max.
-            float m_use = m_new > m_run + 8.0f ? m_new : m_run;
-            // A row with no allowed key yet (only padding rows) keeps a finite point.
-            if (m_use == -INFINITY) m_use = 0.0f;
-            const float alpha = m_use == m_run ? 1.0f : ex2(m_run - m_use);
-            const float neg_m = -m_use;
-            float e_sum;
-            if (single) {
-                // One key block holds the whole row: sum first, then normalise and
-                // round (the exponentials are recomputed from the intact S).
-                e_sum = fast ? score_row_exp<true, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
-                             : score_row_exp<false, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
-                if (fast) {
-                    score_row_exp<true, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
-                } else {
-                    score_row_exp<false, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
-                }
+            float m_use, alpha, e_sum;
+            if (fast && !single) {
+                uint32_t r[128];
+                load_row128(s_addr, r);
+                next_point(m_run, row_max128(r) * c_eff, m_use, alpha);
+                e_sum = row_exp_store128(s_addr, r, c_eff, -m_use);
             } else {
-                e_sum = fast ? score_row_exp<true, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
-                             : score_row_exp<false, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                const float m_raw = fast ? score_row_max<true>(s_addr, limit, pos_scale, c_in)
+                                         : score_row_max<false>(s_addr, limit, pos_scale, c_in);
+                next_point(m_run, m_raw * c_eff, m_use, alpha);
+                const float neg_m = -m_use;
+                if (single) {
+                    // One key block holds the whole row: sum first, then normalise and
+                    // round (the exponentials are recomputed from the intact S).
+                    e_sum = fast ? score_row_exp<true, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
+                                 : score_row_exp<false, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                    if (fast) {
+                        score_row_exp<true, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                    } else {
+                        score_row_exp<false, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                    }
+                } else {
+                    e_sum = score_row_exp<false, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                }
             }
             // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp
             // when any of its rows needs it (alpha == 1 rows multiply by one).
