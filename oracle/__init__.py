@@ -9,6 +9,10 @@ reference's host oracles (see ``tk_oracle.h`` for the file:line each follows).
 ``ref_lib()`` loads ``oracle/_ref/libtk_ref.so`` when present: the reference's own
 host oracle functions compiled from its sources by ``make -C oracle ref``. The
 golden fixtures in ``tests/golden/`` were produced from that library.
+``legacy_lib()`` loads ``oracle/_ref/libtk_legacy.so`` when present: the reference's
+own GEMM and attention kernels built as compute_75 PTX (``make -C oracle legacy``),
+which the driver JIT-compiles for the GPU at hand. It is the legacy-path comparison
+datapoint: it runs the reference's SM7x code on the same device, never the product.
 """
 
 from __future__ import annotations
@@ -23,10 +27,12 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libtk_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libtk_ref.so")
+LEGACY_SO = os.path.join(HERE, "_ref", "libtk_legacy.so")
 
 _lock = threading.Lock()
 _lib = None
 _ref = None
+_legacy = None
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
@@ -37,7 +43,7 @@ def build(ref: bool = False) -> None:
     """Compile the oracle (and, if asked and the reference tree exists, _ref)."""
     targets = ["all"]
     if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference")):
-        targets.append("ref")
+        targets += ["ref", "legacy"]
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
 
@@ -122,6 +128,22 @@ def ref_lib():
             _ref.tkref_diff_model_case.argtypes = [C.c_int, C.POINTER(C.c_int)]
             _ref.tkref_corr_sentinel.restype = C.c_float
         return _ref
+
+
+def legacy_lib():
+    """The reference's GEMM / attention kernels as JIT-compiled PTX (the legacy SM7x
+    path on the current device), or None when oracle/_ref was not built."""
+    global _legacy
+    with _lock:
+        if _legacy is None and os.path.exists(LEGACY_SO):
+            handle = C.CDLL(LEGACY_SO)
+            handle.tkl_gemm_f16_f16_f32_nn.restype = C.c_int
+            handle.tkl_gemm_f16_f16_f32_nn.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_int,
+                                                       C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+            handle.tkl_attention_forward_16x16.restype = C.c_int
+            handle.tkl_attention_forward_16x16.argtypes = [C.c_void_p] * 4 + [C.c_int, C.c_void_p]
+            _legacy = handle
+        return _legacy
 
 
 def _ptr(arr: np.ndarray):
