@@ -164,7 +164,7 @@ def max_over_ranks(value: float, world: int) -> float:
 class Workload:
     """Device-resident inputs and the list of (name, launch, flops_or_bytes) calls of one step."""
 
-    def __init__(self, kind: str, rank: int, world: int):
+    def __init__(self, kind: str, rank: int, world: int, row_tiles: int = ROW_TILES):
         import torch
         import tk_b200
         self.kind = kind
@@ -200,14 +200,14 @@ class Workload:
             self.d2h += [self.o, self.oc]
         if kind == "rowops":
             gen.manual_seed(1 + 1000 * rank)
-            self.tiles = torch.randn(ROW_TILES * 256, device="cuda", generator=gen) * 2
-            self.rs = torch.empty(ROW_TILES * 16, device="cuda")
-            self.rm = torch.empty(ROW_TILES * 16, device="cuda")
-            self.sm = torch.empty(ROW_TILES * 256, device="cuda")
-            self.cs = torch.empty(ROW_TILES * 256, device="cuda")
-            nbytes = ROW_TILES * 1024 * 3 + ROW_TILES * 128
+            self.tiles = torch.randn(row_tiles * 256, device="cuda", generator=gen) * 2
+            self.rs = torch.empty(row_tiles * 16, device="cuda")
+            self.rm = torch.empty(row_tiles * 16, device="cuda")
+            self.sm = torch.empty(row_tiles * 256, device="cuda")
+            self.cs = torch.empty(row_tiles * 256, device="cuda")
+            nbytes = row_tiles * 1024 * 3 + row_tiles * 128
             self.calls.append(("tile_row_ops_all4", lambda: self.tk.row_ops_raw(
-                self.tiles, ROW_TILES, self.rs, self.rm, self.sm, self.cs), float(nbytes), 1))
+                self.tiles, row_tiles, self.rs, self.rm, self.sm, self.cs), float(nbytes), 1))
             self.h2d += [self.tiles]
             self.d2h += [self.rs, self.rm, self.sm, self.cs]
 
@@ -224,7 +224,7 @@ class Workload:
 
 def run_ours(args, rank, world, local):
     import torch
-    wl = Workload(args.workload, rank, world)
+    wl = Workload(args.workload, rank, world, args.row_tiles)
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -261,7 +261,7 @@ def run_ours(args, rank, world, local):
     # device buffer sets and separate copy streams let step i's kernels overlap the
     # host->device copy of step i+1 and the device->host copy of step i-1 (the PCIe
     # directions are independent), as a pipelined host application would run.
-    wl2 = Workload(args.workload, rank, world)
+    wl2 = Workload(args.workload, rank, world, args.row_tiles)
     sets = [wl, wl2]
     # One pinned host copy of the inputs and one of the outputs serve both device
     # sets: copies in one direction are serialised on their stream.
@@ -445,7 +445,11 @@ def main_ours(args):
     name, _, work, _ = wl.calls[dom]
     achieved = work / (per_kernel_ms[dom] / 1e3) / metric_scale
     peak = peaks.get(peak_key, FALLBACK_PEAKS[peak_key])
-    traffic_bytes = traffic.get(name, {}).get("dram_bytes_per_launch") if traffic else None
+    entry = traffic.get(name, {}) if traffic else {}
+    traffic_bytes = entry.get("dram_bytes_per_launch")
+    if traffic_bytes is None and "dram_bytes_per_tile" in entry:
+        # Captured on a smaller tile count; DRAM traffic scales with the tiles processed.
+        traffic_bytes = round(entry["dram_bytes_per_tile"] * args.row_tiles)
     roofline = {"kernel": name, "bound": "hbm" if unit == "GB/s" else "tensor", "achieved": round(achieved, 1),
                 "peak": peak, "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic_bytes,
                 "peak_source": f"{peak_src} {peak_key}"}
@@ -471,8 +475,8 @@ def main_ours(args):
                                      "unmasked + causal, per GPU",
                          "gemm": "GEMM f16 8192x8192x8192 -> f32, per GPU",
                          "attention": "attention fwd [8,32,4096,128] unmasked + causal, per GPU",
-                         "rowops": "1,048,576 16x16 FP32 tiles, sum+max+softmax+causal in one pass, per GPU"}[
-                args.workload],
+                         "rowops": f"{args.row_tiles:,} 16x16 FP32 tiles, sum+max+softmax+causal in one pass, "
+                                   "per GPU"}[args.workload],
             "parallelism": f"dp{world} (GEMM by M row blocks, attention by batch x head, row ops by tile range)",
             "l2": "inputs larger than L2 (126 MB): no flush needed",
             "gather": bool(args.gather),
@@ -564,6 +568,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["headline", "gemm", "attention", "rowops"], default="headline")
     ap.add_argument("--gather", action="store_true", help="NCCL all-gather of each step's outputs")
+    ap.add_argument("--row-tiles", type=int, default=ROW_TILES,
+                    help="tiles per GPU of the rowops workload (default 1,048,576; inputs stay larger than L2 "
+                         "above 126,000)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

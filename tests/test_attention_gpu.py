@@ -108,8 +108,8 @@ def general_case(b, h, s, d, causal, seed, rows=None, pairs=None, misaligned=Fal
 
 
 @pytest.mark.parametrize("shape", [
-    (1, 2, 16, 16), (1, 1, 100, 64), (2, 3, 128, 128), (1, 2, 300, 64), (1, 2, 257, 32),
-    (1, 1, 1000, 128), (1, 1, 129, 128), (2, 1, 640, 16)],
+    (1, 2, 16, 16), (2, 3, 7, 16), (1, 1, 1, 16), (1, 1, 17, 16), (1, 1, 100, 64), (2, 3, 128, 128),
+    (1, 2, 300, 64), (1, 2, 257, 32), (1, 1, 1000, 128), (1, 1, 129, 128), (2, 1, 640, 16)],
     ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("causal", [False, True])
 def test_general_shapes(shape, causal):
@@ -132,10 +132,11 @@ def test_large_8x32x4096x128_sampled(causal):
 
 
 @pytest.mark.parametrize("causal", [False, True])
-@pytest.mark.parametrize("heads_q,heads_kv", [(8, 2), (4, 1), (6, 3)])
-def test_grouped_query_attention(heads_q, heads_kv, causal):
+@pytest.mark.parametrize("heads_q,heads_kv,s,d", [(8, 2, 300, 64), (4, 1, 300, 64), (6, 3, 300, 64),
+                                                  (4, 2, 16, 16), (6, 2, 9, 16)])
+def test_grouped_query_attention(heads_q, heads_kv, s, d, causal):
     """Query head h attends with key/value head h / (heads_q / heads_kv)."""
-    b, s, d = 2, 300, 64
+    b = 2
     group = heads_q // heads_kv
     q, _, _ = oracle.gen_qkv_normal(40 + heads_q, 1.0, b * heads_q * s * d)
     _, k, v = oracle.gen_qkv_normal(50 + heads_kv, 1.0, b * heads_kv * s * d)

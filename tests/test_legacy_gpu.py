@@ -86,25 +86,48 @@ def _time(fn, iters):
     return start.elapsed_time(stop) / iters
 
 
+def _best_of(fn, reps=5, warm=2):
+    """The reference's bench method (bench/gemm_throughput.cu:94-120): best of
+    `reps` event-timed calls after `warm` warm-up calls, in ms."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    best = math.inf
+    for _ in range(reps):
+        best = min(best, _time(fn, 1))
+    return best
+
+
 def test_legacy_path_datapoint():
-    """GEMM 8192^3 and the one-tile attention through both paths on this GPU."""
+    """GEMM at the reference bench's square sizes (bench/gemm_throughput.cu:22-30, plus
+    256 and 8192) and the one-tile attention per public call
+    (bench/attention_throughput.cu:128-165), through both paths on this GPU."""
     lib = legacy()
-    m = n = k = 8192
     gen = torch.Generator(device="cuda").manual_seed(2)
-    a = (torch.rand(m, k, device="cuda", generator=gen) * 2 - 1).half()
-    b = (torch.rand(k, n, device="cuda", generator=gen) * 2 - 1).half()
-    c = torch.empty(m, n, device="cuda")
-    flops = 2.0 * m * n * k
-    ms_legacy = _time(lambda: lib.tkl_gemm_f16_f16_f32_nn(m, n, k, a.data_ptr(), k, b.data_ptr(), n,
-                                                           c.data_ptr(), n, None), 3)
-    ms_native = _time(lambda: tk_b200.gemm_raw(m, n, k, a, k, b, n, c, n), 10)
+    lines = [f"legacy-path datapoint on {torch.cuda.get_device_name()}"]
+    native_8192 = legacy_8192 = None
+    for size in (256, 512, 1024, 2048, 4096, 8192):
+        m = n = k = size
+        a = (torch.rand(m, k, device="cuda", generator=gen) * 2 - 1).half()
+        b = (torch.rand(k, n, device="cuda", generator=gen) * 2 - 1).half()
+        c = torch.empty(m, n, device="cuda")
+        flops = 2.0 * m * n * k
+        ms_legacy = _best_of(lambda: lib.tkl_gemm_f16_f16_f32_nn(m, n, k, a.data_ptr(), k, b.data_ptr(), n,
+                                                                  c.data_ptr(), n, None),
+                             reps=3 if size == 8192 else 5)
+        ms_native = _best_of(lambda: tk_b200.gemm_raw(m, n, k, a, k, b, n, c, n))
+        lines.append(f"  GEMM {size}^3: legacy {1e3 * ms_legacy:9.1f} us {flops / ms_legacy / 1e9:8.1f} TFLOP/s | "
+                     f"sm_100a {1e3 * ms_native:8.1f} us {flops / ms_native / 1e9:8.1f} TFLOP/s | "
+                     f"x{ms_legacy / ms_native:.1f}")
+        if size == 8192:
+            native_8192, legacy_8192 = ms_native, ms_legacy
     q = torch.zeros(256, dtype=torch.float16, device="cuda")
     out = torch.empty(256, device="cuda")
-    us_legacy = 1e3 * _time(lambda: lib.tkl_attention_forward_16x16(q.data_ptr(), q.data_ptr(), q.data_ptr(),
-                                                                      out.data_ptr(), 0, None), 200)
-    us_native = 1e3 * _time(lambda: tk_b200.attention_16x16_raw(q, q, q, out, False), 200)
-    print(f"\nlegacy-path datapoint on {torch.cuda.get_device_name()}: GEMM 8192^3 "
-          f"legacy {flops / ms_legacy / 1e9:.1f} TFLOP/s ({ms_legacy:.2f} ms) vs sm_100a "
-          f"{flops / ms_native / 1e9:.1f} TFLOP/s ({ms_native:.3f} ms); attention 16x16 per call "
-          f"legacy {us_legacy:.1f} us vs sm_100a {us_native:.1f} us")
-    assert math.isfinite(ms_legacy) and ms_native < ms_legacy
+    for causal in (0, 1):
+        us_legacy = 1e3 * _time(lambda: lib.tkl_attention_forward_16x16(q.data_ptr(), q.data_ptr(), q.data_ptr(),
+                                                                          out.data_ptr(), causal, None), 2000)
+        us_native = 1e3 * _time(lambda: tk_b200.attention_16x16_raw(q, q, q, out, bool(causal)), 2000)
+        lines.append(f"  attention 16x16{' causal' if causal else ''} per call: legacy {us_legacy:.2f} us | "
+                     f"sm_100a {us_native:.2f} us")
+    print("\n" + "\n".join(lines))
+    assert math.isfinite(legacy_8192) and native_8192 < legacy_8192

@@ -578,6 +578,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// One-tile attention (S <= 16 keys, head_dim 16): the shape of the reference's
+// attention_forward_16x16 (src/attention.cu:10-60). 16 x 16 x 16 is below the
+// smallest tcgen05 tile (M = 64), and a TMEM allocation, three tensor maps and a
+// TMA pipeline cost several times the arithmetic, so this latency path runs on
+// the FP32 pipe: one CTA of 256 threads per (batch, head), thread (i, j) owns
+// score S[i][j] and output O[i][j]. Products of binary16 values are exact in
+// FP32, so the dot products follow the same model as an FP32-accumulating MMA.
+// Row max and sum use xor shuffles over the row's 16 lanes; P = rn16(e / l) with
+// the row's final sum, the reference's normalise-then-round (src/attention.cu:38-47).
+constexpr int kTileThreads = 256;
+
+__global__ void __launch_bounds__(kTileThreads)
+    attention_tile16_kernel(const __half* __restrict__ q, const __half* __restrict__ k,
+                            const __half* __restrict__ v, float* __restrict__ out, int seq, int heads_q,
+                            int heads_kv, int group, float scale, int causal) {
+    __shared__ float qs[16][17], ks[16][17], vs[16][17], ps[16][17];
+    const int t = static_cast<int>(threadIdx.x);
+    const int i = t >> 4;  // query row; also the row of the element this thread loads
+    const int j = t & 15;  // key index for S, output column for O
+    const int bh = static_cast<int>(blockIdx.x);
+    const int bh_kv = (bh / heads_q) * heads_kv + (bh % heads_q) / group;
+    const long long q_base = static_cast<long long>(bh) * seq * 16;
+    const long long kv_base = static_cast<long long>(bh_kv) * seq * 16;
+    const bool row_valid = i < seq;
+    qs[i][j] = row_valid ? __half2float(q[q_base + t]) : 0.0f;
+    ks[i][j] = row_valid ? __half2float(k[kv_base + t]) : 0.0f;
+    vs[i][j] = row_valid ? __half2float(v[kv_base + t]) : 0.0f;
+    __syncthreads();
+
+    float s = 0.0f;
+#pragma unroll
+    for (int d = 0; d < 16; ++d) s = fmaf(qs[i][d], ks[j][d], s);
+    const bool masked = j >= seq || (causal && j > i);
+    const float x = masked ? -INFINITY : s * scale;
+    // Key 0 is never masked (seq >= 1), so every row has a finite max.
+    float m = x;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o, 16));
+    const float e = masked ? 0.0f : ex2((x - m) * 1.4426950408889634f);
+    float l = e;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o, 16);
+    ps[i][j] = __half2float(__float2half_rn(__fdiv_rn(e, l)));
+    __syncthreads();
+
+    float o_acc = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) o_acc = fmaf(ps[i][u], vs[u][j], o_acc);
+    if (row_valid) out[q_base + t] = o_acc;
+}
+
 __global__ void repack_kernel(const uint16_t* src, uint16_t* dst, long long count) {
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
          i += static_cast<long long>(gridDim.x) * blockDim.x)
@@ -639,6 +690,14 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
     cudaError_t err = host::current_device(&device, nullptr);
     if (err != cudaSuccess) return err;
     static_cast<void>(cudaGetLastError());
+
+    if (head_dim == 16 && seq <= 16) {
+        // One tile per (batch, head): the latency path (no alignment needs beyond binary16).
+        attention_tile16_kernel<<<static_cast<unsigned>(batch * heads), kTileThreads, 0, stream>>>(
+            static_cast<const __half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v), out,
+            seq, heads, heads_kv, heads / heads_kv, scale, causal);
+        return cudaGetLastError();
+    }
 
     Params p{};
     p.seq = seq;
