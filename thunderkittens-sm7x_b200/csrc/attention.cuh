@@ -167,8 +167,8 @@ __device__ __forceinline__ float score_row_max(uint32_t s_addr, int limit, bool 
 }
 
 // Exponentials 2^(s * c_eff - m) of the row, chunk by chunk, with the next chunk's
-// TMEM load in flight while the current one is computed (masked blocks and the
-// single-block path; unmasked blocks take row_exp_store128). kMode 0: write binary16 P (over
+// TMEM load in flight while the current one is computed (the single-block path
+// and a non-positive scale; the others take row_exp_store128). kMode 0: write binary16 P (over
 // the S columns already consumed) and return the sum; 1: only return the sum;
 // 2: write binary16 P / norm (exact normalise-then-round of a single key block).
 template <bool kFast, int kMode>
@@ -207,16 +207,23 @@ __device__ __forceinline__ float score_row_exp(uint32_t s_addr, int limit, bool 
     return ((acc[0] + acc[1]) + (acc[2] + acc[3])) + ((acc[4] + acc[5]) + (acc[6] + acc[7]));
 }
 
-// Fast path of a block with no masked key and a positive scale: the thread's
-// whole 128-score row comes into registers with one TMEM round trip (four loads
-// in flight, one wait); the max, the exponentials, their sum and the binary16 P
-// are then computed from registers.
+// Main path (positive scale, more than one key block): the thread's whole
+// 128-score row comes into registers with one TMEM round trip (four loads in
+// flight, one wait); masking, the max, the exponentials, their sum and the
+// binary16 P are then computed from registers.
 __device__ __forceinline__ void load_row128(uint32_t s_addr, uint32_t (&r)[128]) {
     tmem_ld_32x32b_x32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
     tmem_ld_32x32b_x32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
     tmem_ld_32x32b_x32(s_addr + 64, *reinterpret_cast<uint32_t(*)[32]>(&r[64]));
     tmem_ld_32x32b_x32(s_addr + 96, *reinterpret_cast<uint32_t(*)[32]>(&r[96]));
     tmem_wait_ld();
+}
+
+// Keys at column >= limit are masked: their scores become -inf.
+__device__ __forceinline__ void mask_row128(uint32_t (&r)[128], int limit) {
+#pragma unroll
+    for (int i = 0; i < 128; ++i)
+        if (i >= limit) r[i] = 0xff800000u;  // -inf
 }
 
 __device__ __forceinline__ float row_max128(const uint32_t (&r)[128]) {
@@ -301,6 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool has_tile1 = q0 + kBlockQ < p.seq;
     const int kv_end = p.causal ? min(p.seq, q0 + (has_tile1 ? 2 : 1) * kBlockQ) : p.seq;
     const int n_blocks = (kv_end + kBlockKV - 1) / kBlockKV;
+    // Causal with two tiles: the last key block starts at or after q0 + 128, past
+    // every row of tile 0, so tile 0 stops one block early (it would be all masked).
+    const int n_blocks0 = (p.causal && has_tile1) ? n_blocks - 1 : n_blocks;
     const bool single = p.seq <= kBlockKV;
 
     if (threadIdx.x == 0) {
@@ -411,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int v_slot = (2 * j + 1) % kKvSlots;
                 const int prev_v_slot = (2 * j - 1 + kKvSlots) % kKvSlots;
                 const bool last = j == n_blocks - 1;
+                const bool tile0 = j < n_blocks0;
                 // PV1_{j-1}, then V_{j-1} is free
                 if (j > 0) {
                     if (has_tile1) {
@@ -421,22 +432,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     mma_commit(kv_empty(prev_v_slot));
                 }
-                // S1_j, then K_j is free
+                // S1_j, then K_j is free. K_j was waited for before S0_j, unless
+                // tile 0 has already finished.
+                if (!tile0 && !mbar_wait(kv_full(k_slot), kv_phase(2 * j), kFaultAttnWait, abort_flag)) break;
                 if (has_tile1) issue_s(1, kv_addr(k_slot));
                 mma_commit(kv_empty(k_slot));
                 // PV0_j and S0_{j+1}, back to back
                 if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
-                const int next_k_slot = (2 * j + 2) % kKvSlots;
-                if (!last && !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
-                    break;
-                if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
-                pr_phase[0] ^= 1u;
-                tc_fence_after();
-                issue_pv(0, kv_addr(v_slot), j == 0);
-                if (last) {
-                    mma_commit(o_final(0));
-                } else {
-                    issue_s(0, kv_addr(next_k_slot));
+                if (tile0) {
+                    const bool tile0_last = j == n_blocks0 - 1;
+                    const int next_k_slot = (2 * j + 2) % kKvSlots;
+                    if (!tile0_last &&
+                        !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
+                        break;
+                    if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
+                    pr_phase[0] ^= 1u;
+                    tc_fence_after();
+                    issue_pv(0, kv_addr(v_slot), j == 0);
+                    if (tile0_last) {
+                        mma_commit(o_final(0));
+                    } else {
+                        issue_s(0, kv_addr(next_k_slot));
+                    }
                 }
                 if (last) {
                     // PV1_last
@@ -465,7 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m_run = -INFINITY;  // running max, log2 units
         float l_run = 0.0f;       // running sum of exp2(s - m_run)
         bool ok = active;
-        for (int j = 0; j < n_blocks && ok; ++j) {
+        const int my_blocks = g == 0 ? n_blocks0 : n_blocks;
+        for (int j = 0; j < my_blocks && ok; ++j) {
             if (!mbar_wait_warp(s_full(g), static_cast<uint32_t>(j) & 1u, kFaultAttnWait, abort_flag)) {
                 ok = false;
                 break;
@@ -478,16 +496,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool need_mask = __any_sync(0xffffffffu, limit < kBlockKV);
             // Scores in log2 units are s * c. For c > 0 the max of the raw scores is
             // scaled once and each exponent argument is a single FMA; otherwise the
-            // scores are scaled first. Blocks with no masked key take a branch-free
-            // path (the choice is warp-uniform).
+            // scores are scaled first. Masking runs only for blocks where some row
+            // of the warp has a masked key (the choice is warp-uniform).
             const float c_in = p.scale_log2;
             const bool pos_scale = c_in > 0.0f;
             const float c_eff = pos_scale ? c_in : 1.0f;
             const bool fast = pos_scale && !need_mask;
             float m_use, alpha, e_sum;
-            if (fast && !single) {
+            if (pos_scale && !single) {
+                // Whole row in registers. Masked keys (causal diagonal, sequence
+                // tail) become -inf in place, so their exponentials are exactly 0.
                 uint32_t r[128];
                 load_row128(s_addr, r);
+                if (need_mask) mask_row128(r, limit);
                 next_point(m_run, row_max128(r) * c_eff, m_use, alpha);
                 e_sum = row_exp_store128(s_addr, r, c_eff, -m_use);
             } else {
