@@ -152,3 +152,11 @@ def test_grouped_query_attention(heads_q, heads_kv, s, d, causal):
         want = oracle.attention_ref(qs[bh], ks[kv], vs[kv], s, d, scale, causal)
         bound = oracle.attention_bound(vs[kv], s, d)
         assert np.all(np.abs(got[bh] - want) <= bound[None, :]), bh
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_more_items_than_sms_every_head(causal):
+    """300 (batch, head) items of one query-tile pair each: more work items than SMs,
+    so the persistent CTAs take items from the shared counter and run several items
+    each; every output row of every head is checked."""
+    general_case(1, 300, 256, 64, causal, seed=7)

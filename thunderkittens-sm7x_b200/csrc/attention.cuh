@@ -77,6 +77,8 @@ struct Params {
     int causal;
     float* out;
     bool out_vec4;
+    int num_items;      // bh * pairs work items, item w = (bh w / pairs, pair pairs - 1 - w % pairs)
+    int* next_item;     // zeroed counter for dynamic scheduling, or null: item w -> CTA w % grid
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -277,6 +279,37 @@ __device__ __forceinline__ void next_point(float m_run, float m_blk, float& m_us
     alpha = m_use == m_run ? 1.0f : ex2(m_run - m_use);
 }
 
+// Geometry of work item w: one (batch, head) and a pair of 128-row query tiles.
+// Within a (batch, head) the items run heaviest first (later query pairs see more
+// keys under causal masking), and the items of one (batch, head) are adjacent, so
+// the CTAs running at one time share its K and V blocks through L2.
+struct Item {
+    int bh, bh_kv, q0, n_blocks, n_blocks0;
+    bool has_tile1;
+};
+
+__device__ __forceinline__ Item make_item(int w, const Params& p) {
+    Item it;
+    const int pair = p.pairs - 1 - w % p.pairs;
+    it.bh = w / p.pairs;
+    // Key/value slice: query head h of batch b reads key/value head h / group.
+    it.bh_kv = (it.bh / p.heads_q) * p.heads_kv + (it.bh % p.heads_q) / p.group;
+    it.q0 = pair * 2 * kBlockQ;
+    it.has_tile1 = it.q0 + kBlockQ < p.seq;
+    const int kv_end = p.causal ? min(p.seq, it.q0 + (it.has_tile1 ? 2 : 1) * kBlockQ) : p.seq;
+    it.n_blocks = (kv_end + kBlockKV - 1) / kBlockKV;
+    // Causal with two tiles: the last key block starts at or after q0 + 128, past
+    // every row of tile 0, so tile 0 stops one block early (it would be all masked).
+    it.n_blocks0 = (p.causal && it.has_tile1) ? it.n_blocks - 1 : it.n_blocks;
+    return it;
+}
+
+// Persistent: each CTA loops over work items. The TMA warp fetches the next item
+// number (a counter in global memory, or a static stride when the grid covers all
+// items), publishes it to the other roles through a two-entry ring in shared memory,
+// and prefetches the item's Q and first K/V blocks while the previous item's last
+// blocks and its output are still being processed. Barrier phases continue across
+// items.
 template <int kDPad>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -289,28 +322,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t bars = base + C::kBarOffset;
     auto kv_full = [&](int s) { return bars + 8u * s; };
     auto kv_empty = [&](int s) { return bars + 8u * (kKvSlots + s); };
-    const uint32_t q_full = bars + 8u * (2 * kKvSlots);
-    auto s_full = [&](int g) { return bars + 8u * (2 * kKvSlots + 1 + g); };
-    auto p_ready = [&](int g) { return bars + 8u * (2 * kKvSlots + 3 + g); };
-    auto o_final = [&](int g) { return bars + 8u * (2 * kKvSlots + 5 + g); };
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * (2 * kKvSlots + 7));
+    constexpr int kB = 2 * kKvSlots;
+    const uint32_t q_full = bars + 8u * kB;
+    const uint32_t q_empty = bars + 8u * (kB + 1);
+    auto s_full = [&](int g) { return bars + 8u * (kB + 2 + g); };
+    auto p_ready = [&](int g) { return bars + 8u * (kB + 4 + g); };
+    auto o_final = [&](int g) { return bars + 8u * (kB + 6 + g); };
+    auto o_empty = [&](int g) { return bars + 8u * (kB + 8 + g); };
+    auto item_full = [&](int s) { return bars + 8u * (kB + 10 + s); };
+    auto item_empty = [&](int s) { return bars + 8u * (kB + 12 + s); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kBarOffset + 8 * (kB + 14));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* item_info = reinterpret_cast<volatile int*>(tmem_slot + 2);  // two entries
 
     const uint32_t warp = warp_id();
     const uint32_t lane = lane_id();
-
-    // Heaviest causal work first: later query pairs see more keys.
-    const int pair = p.pairs - 1 - static_cast<int>(blockIdx.x % p.pairs);
-    const int bh = static_cast<int>(blockIdx.x / p.pairs);
-    // Key/value slice: query head h of batch b reads key/value head h / group.
-    const int bh_kv = (bh / p.heads_q) * p.heads_kv + (bh % p.heads_q) / p.group;
-    const int q0 = pair * 2 * kBlockQ;
-    const bool has_tile1 = q0 + kBlockQ < p.seq;
-    const int kv_end = p.causal ? min(p.seq, q0 + (has_tile1 ? 2 : 1) * kBlockQ) : p.seq;
-    const int n_blocks = (kv_end + kBlockKV - 1) / kBlockKV;
-    // Causal with two tiles: the last key block starts at or after q0 + 128, past
-    // every row of tile 0, so tile 0 stops one block early (it would be all masked).
-    const int n_blocks0 = (p.causal && has_tile1) ? n_blocks - 1 : n_blocks;
     const bool single = p.seq <= kBlockKV;
 
     if (threadIdx.x == 0) {
@@ -319,10 +345,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(kv_empty(s), 1);
         }
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int g = 0; g < 2; ++g) {
             mbar_init(s_full(g), 1);
             mbar_init(p_ready(g), 4);
             mbar_init(o_final(g), 1);
+            mbar_init(o_empty(g), 4);
+            mbar_init(item_full(g), 1);
+            mbar_init(item_empty(g), 9);  // the MMA thread and the eight softmax warps
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -337,43 +367,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 8) {
-        // ---------------- TMA producer (one thread) ----------------
+        // ---------------- TMA producer and scheduler (one thread) ----------------
         if (lane == 0) {
             tma_prefetch_desc(&map_q);
             tma_prefetch_desc(&map_k);
             tma_prefetch_desc(&map_v);
-            const int ntiles = has_tile1 ? 2 : 1;
-            mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
-            for (int g = 0; g < ntiles; ++g)
-                for (int x = 0; x < C::kBoxes; ++x)
-                    tma_load_3d(base + C::kQOffset + g * C::kTileBytes + x * 16384, &map_q, q_full,
-                                x * 64, q0 + g * kBlockQ, bh);
             int slot = 0;
             uint32_t phase = 0;
             int issued = 0;
+            int items = 0;
             bool ok = true;
-            for (int j = 0; j < n_blocks && ok; ++j) {
-                for (int which = 0; which < 2; ++which) {  // K then V
-                    if (!mbar_wait(kv_empty(slot), phase ^ 1u, kFaultProducerWait, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t dst = base + C::kKvOffset + slot * C::kTileBytes;
-                    mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
+            int w = static_cast<int>(blockIdx.x);
+            for (int it_slot = 0;; it_slot ^= 1) {
+                if (items > 0) {
+                    w = p.next_item != nullptr ? static_cast<int>(gridDim.x) + atomicAdd(p.next_item, 1)
+                                               : w + static_cast<int>(gridDim.x);
+                }
+                const int wi = w < p.num_items ? w : -1;
+                // Entry it_slot was last used two items ago.
+                if (items >= 2 &&
+                    !mbar_wait(item_empty(it_slot), static_cast<uint32_t>((items - 2) >> 1) & 1u,
+                               kFaultProducerWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                item_info[it_slot] = wi;
+                mbar_arrive(item_full(it_slot));
+                if (wi < 0) break;
+                const Item it = make_item(wi, p);
+                // Q of the previous item is free once all its S MMAs have completed.
+                if (items > 0 &&
+                    !mbar_wait(q_empty, static_cast<uint32_t>(items - 1) & 1u, kFaultProducerWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                const int ntiles = it.has_tile1 ? 2 : 1;
+                mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
+                for (int g = 0; g < ntiles; ++g)
                     for (int x = 0; x < C::kBoxes; ++x)
-                        tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
-                                    x * 64, j * kBlockKV, bh_kv);
-                    ++issued;
-                    if (++slot == kKvSlots) {
-                        slot = 0;
-                        phase ^= 1u;
+                        tma_load_3d(base + C::kQOffset + g * C::kTileBytes + x * 16384, &map_q, q_full,
+                                    x * 64, it.q0 + g * kBlockQ, it.bh);
+                ++items;
+                for (int j = 0; j < it.n_blocks && ok; ++j) {
+                    for (int which = 0; which < 2; ++which) {  // K then V
+                        if (!mbar_wait(kv_empty(slot), phase ^ 1u, kFaultProducerWait, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t dst = base + C::kKvOffset + slot * C::kTileBytes;
+                        mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
+                        for (int x = 0; x < C::kBoxes; ++x)
+                            tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
+                                        x * 64, j * kBlockKV, it.bh_kv);
+                        ++issued;
+                        if (++slot == kKvSlots) {
+                            slot = 0;
+                            phase ^= 1u;
+                        }
                     }
                 }
+                if (!ok) break;
             }
             if (!ok) {
-                // Let every issued load land before the CTA may exit: wait for the
-                // full-barrier phase of each of the last (up to kKvSlots) loads.
-                mbar_wait(q_full, 0, kFaultDrainWait, nullptr);
+                // Let every issued load land before the CTA may exit: the last Q load
+                // and the last (up to kKvSlots) K/V loads.
+                if (items > 0) mbar_wait(q_full, static_cast<uint32_t>(items - 1) & 1u, kFaultDrainWait, nullptr);
                 int s = slot;
                 uint32_t ph = phase;
                 for (int i = 0; i < min(issued, kKvSlots); ++i) {
@@ -394,7 +452,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
             auto kv_addr = [&](int slot) { return base + C::kKvOffset + slot * C::kTileBytes; };
-            auto kv_phase = [&](int load) { return static_cast<uint32_t>(load / kKvSlots) & 1u; };
             auto issue_s = [&](int g, uint32_t k_addr) {
 #pragma unroll
                 for (int kk = 0; kk < kDPad / 16; ++kk) {
@@ -412,60 +469,92 @@ __global__ void __launch_bounds__(kThreads, 1)
                                (!first || kk > 0) ? 1u : 0u);
             };
             uint32_t pr_phase[2] = {0, 0};
-            bool ok = mbar_wait(q_full, 0, kFaultAttnWait, abort_flag) &&
-                      mbar_wait(kv_full(0), 0, kFaultAttnWait, abort_flag);
-            tc_fence_after();
-            if (ok) issue_s(0, kv_addr(0));
-            for (int j = 0; j < n_blocks && ok; ++j) {
-                const int k_slot = (2 * j) % kKvSlots;
-                const int v_slot = (2 * j + 1) % kKvSlots;
-                const int prev_v_slot = (2 * j - 1 + kKvSlots) % kKvSlots;
-                const bool last = j == n_blocks - 1;
-                const bool tile0 = j < n_blocks0;
-                // PV1_{j-1}, then V_{j-1} is free
-                if (j > 0) {
-                    if (has_tile1) {
-                        if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                        pr_phase[1] ^= 1u;
+            int done[2] = {0, 0};  // items in which tile g has produced an output
+            int kv_base = 0;       // K/V loads of the previous items
+            int items = 0;
+            bool ok = true;
+            // The first PV of tile g in an item overwrites O_g: the softmax warps must
+            // have read the previous item's O_g out of tensor memory.
+            auto o_free = [&](int g) {
+                return done[g] == 0 ||
+                       mbar_wait(o_empty(g), static_cast<uint32_t>(done[g] - 1) & 1u, kFaultAttnWait, abort_flag);
+            };
+            for (int it_slot = 0; ok; it_slot ^= 1, ++items) {
+                if (!mbar_wait(item_full(it_slot), static_cast<uint32_t>(items >> 1) & 1u, kFaultAttnWait,
+                               abort_flag))
+                    break;
+                const int wi = item_info[it_slot];
+                mbar_arrive(item_empty(it_slot));
+                if (wi < 0) break;
+                const Item it = make_item(wi, p);
+                auto kv_slot = [&](int load) { return (kv_base + load) % kKvSlots; };
+                auto kv_phase = [&](int load) { return static_cast<uint32_t>((kv_base + load) / kKvSlots) & 1u; };
+                ok = mbar_wait(q_full, static_cast<uint32_t>(items) & 1u, kFaultAttnWait, abort_flag) &&
+                     mbar_wait(kv_full(kv_slot(0)), kv_phase(0), kFaultAttnWait, abort_flag);
+                tc_fence_after();
+                if (ok) issue_s(0, kv_addr(kv_slot(0)));
+                const int n_blocks = it.n_blocks;
+                for (int j = 0; j < n_blocks && ok; ++j) {
+                    ok = false;
+                    const int k_slot = kv_slot(2 * j);
+                    const int v_slot = kv_slot(2 * j + 1);
+                    const int prev_v_slot = kv_slot(2 * j - 1 + kKvSlots) ;
+                    const bool last = j == n_blocks - 1;
+                    const bool tile0 = j < it.n_blocks0;
+                    // PV1_{j-1}, then V_{j-1} is free
+                    if (j > 0) {
+                        if (it.has_tile1) {
+                            if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                            pr_phase[1] ^= 1u;
+                            if (j == 1 && !o_free(1)) break;
+                            tc_fence_after();
+                            issue_pv(1, kv_addr(prev_v_slot), j == 1);
+                        }
+                        mma_commit(kv_empty(prev_v_slot));
+                    }
+                    // S1_j, then K_j is free. K_j was waited for before S0_j, unless
+                    // tile 0 has already finished.
+                    if (!tile0 && !mbar_wait(kv_full(k_slot), kv_phase(2 * j), kFaultAttnWait, abort_flag)) break;
+                    if (it.has_tile1) issue_s(1, kv_addr(k_slot));
+                    mma_commit(kv_empty(k_slot));
+                    // After the item's last S MMA, Q may be replaced by the next item's.
+                    if (last) mma_commit(q_empty);
+                    // PV0_j and S0_{j+1}, back to back
+                    if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
+                    if (tile0) {
+                        const bool tile0_last = j == it.n_blocks0 - 1;
+                        const int next_k_slot = kv_slot(2 * j + 2);
+                        if (!tile0_last &&
+                            !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
+                            break;
+                        if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
+                        pr_phase[0] ^= 1u;
+                        if (j == 0 && !o_free(0)) break;
                         tc_fence_after();
-                        issue_pv(1, kv_addr(prev_v_slot), j == 1);
+                        issue_pv(0, kv_addr(v_slot), j == 0);
+                        if (tile0_last) {
+                            mma_commit(o_final(0));
+                        } else {
+                            issue_s(0, kv_addr(next_k_slot));
+                        }
                     }
-                    mma_commit(kv_empty(prev_v_slot));
-                }
-                // S1_j, then K_j is free. K_j was waited for before S0_j, unless
-                // tile 0 has already finished.
-                if (!tile0 && !mbar_wait(kv_full(k_slot), kv_phase(2 * j), kFaultAttnWait, abort_flag)) break;
-                if (has_tile1) issue_s(1, kv_addr(k_slot));
-                mma_commit(kv_empty(k_slot));
-                // PV0_j and S0_{j+1}, back to back
-                if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
-                if (tile0) {
-                    const bool tile0_last = j == n_blocks0 - 1;
-                    const int next_k_slot = (2 * j + 2) % kKvSlots;
-                    if (!tile0_last &&
-                        !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
-                        break;
-                    if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
-                    pr_phase[0] ^= 1u;
-                    tc_fence_after();
-                    issue_pv(0, kv_addr(v_slot), j == 0);
-                    if (tile0_last) {
-                        mma_commit(o_final(0));
-                    } else {
-                        issue_s(0, kv_addr(next_k_slot));
+                    if (last) {
+                        // PV1_last
+                        if (it.has_tile1) {
+                            if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                            pr_phase[1] ^= 1u;
+                            if (j == 0 && !o_free(1)) break;
+                            tc_fence_after();
+                            issue_pv(1, kv_addr(v_slot), j == 0);
+                            mma_commit(o_final(1));
+                        }
+                        mma_commit(kv_empty(v_slot));
                     }
+                    ok = true;
                 }
-                if (last) {
-                    // PV1_last
-                    if (has_tile1) {
-                        if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                        pr_phase[1] ^= 1u;
-                        tc_fence_after();
-                        issue_pv(1, kv_addr(v_slot), j == 0);
-                        mma_commit(o_final(1));
-                    }
-                    mma_commit(kv_empty(v_slot));
-                }
+                ++done[0];
+                if (it.has_tile1) ++done[1];
+                kv_base += 2 * n_blocks;
             }
         }
         __syncwarp();
@@ -474,108 +563,127 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = static_cast<int>(warp >> 2);
         const uint32_t quarter = warp & 3u;
         const int row_in_tile = static_cast<int>(quarter * 32 + lane);
-        const int q_row = q0 + g * kBlockQ + row_in_tile;
         const uint32_t lane_bits = (quarter * 32u) << 16;
         const uint32_t s_addr = tmem + lane_bits + 256u * g;
         const uint32_t o_addr = s_addr + 128u;
-        const bool active = g == 0 || has_tile1;
-        float m_run = -INFINITY;  // running max, log2 units
-        float l_run = 0.0f;       // running sum of exp2(s - m_run)
-        bool ok = active;
-        const int my_blocks = g == 0 ? n_blocks0 : n_blocks;
-        for (int j = 0; j < my_blocks && ok; ++j) {
-            if (!mbar_wait_warp(s_full(g), static_cast<uint32_t>(j) & 1u, kFaultAttnWait, abort_flag)) {
+        const float c_in = p.scale_log2;
+        const bool pos_scale = c_in > 0.0f;
+        const float c_eff = pos_scale ? c_in : 1.0f;
+        uint32_t sf_phase = 0;  // s_full(g) completions seen
+        uint32_t of_phase = 0;  // o_final(g) completions seen
+        bool ok = true;
+        for (int it_slot = 0, items = 0; ok; it_slot ^= 1, ++items) {
+            if (!mbar_wait_warp(item_full(it_slot), static_cast<uint32_t>(items >> 1) & 1u, kFaultAttnWait,
+                                abort_flag))
+                break;
+            const int wi = item_info[it_slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(item_empty(it_slot));
+            if (wi < 0) break;
+            const Item it = make_item(wi, p);
+            if (g == 1 && !it.has_tile1) continue;
+            const int q_row = it.q0 + g * kBlockQ + row_in_tile;
+            float m_run = -INFINITY;  // running max, log2 units
+            float l_run = 0.0f;       // running sum of exp2(s - m_run)
+            const int my_blocks = g == 0 ? it.n_blocks0 : it.n_blocks;
+            for (int j = 0; j < my_blocks; ++j) {
+                if (!mbar_wait_warp(s_full(g), sf_phase, kFaultAttnWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                sf_phase ^= 1u;
+                tc_fence_after();
+                const int kv0 = j * kBlockKV;
+                // Keys past the sequence end, and (causal) keys after this query, are masked.
+                int limit = p.seq - kv0;
+                if (p.causal) limit = min(limit, q_row - kv0 + 1);
+                const bool need_mask = __any_sync(0xffffffffu, limit < kBlockKV);
+                // Scores in log2 units are s * c. For c > 0 the max of the raw scores is
+                // scaled once and each exponent argument is a single FMA; otherwise the
+                // scores are scaled first. Masking runs only for blocks where some row
+                // of the warp has a masked key (the choice is warp-uniform).
+                const bool fast = pos_scale && !need_mask;
+                float m_use, alpha, e_sum;
+                if (pos_scale && !single) {
+                    // Whole row in registers. Masked keys (causal diagonal, sequence
+                    // tail) become -inf in place, so their exponentials are exactly 0.
+                    uint32_t r[128];
+                    load_row128(s_addr, r);
+                    if (need_mask) mask_row128(r, limit);
+                    next_point(m_run, row_max128(r) * c_eff, m_use, alpha);
+                    e_sum = row_exp_store128(s_addr, r, c_eff, -m_use);
+                } else {
+                    const float m_raw = fast ? score_row_max<true>(s_addr, limit, pos_scale, c_in)
+                                             : score_row_max<false>(s_addr, limit, pos_scale, c_in);
+                    next_point(m_run, m_raw * c_eff, m_use, alpha);
+                    const float neg_m = -m_use;
+                    if (single) {
+                        // One key block holds the whole row: sum first, then normalise and
+                        // round (the exponentials are recomputed from the intact S).
+                        e_sum = fast ? score_row_exp<true, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
+                                     : score_row_exp<false, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                        if (fast) {
+                            score_row_exp<true, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                        } else {
+                            score_row_exp<false, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
+                        }
+                    } else {
+                        e_sum = score_row_exp<false, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
+                    }
+                }
+                // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp
+                // when any of its rows needs it (alpha == 1 rows multiply by one).
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+                    // Rescale the running output: PV_{j-1} has completed (in-order tcgen05).
+#pragma unroll
+                    for (int c = 0; c < kDPad / 16; ++c) {
+                        uint32_t r[16];
+                        tmem_ld_32x32b_x16(o_addr + 16 * c, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+                        tmem_st_32x32b_x16(o_addr + 16 * c, r);
+                    }
+                }
+                l_run = l_run * alpha + e_sum;
+                m_run = m_use;
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_ready(g));
+            }
+            if (!ok || !mbar_wait_warp(o_final(g), of_phase, kFaultAttnWait, abort_flag)) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            const int kv0 = j * kBlockKV;
-            // Keys past the sequence end, and (causal) keys after this query, are masked.
-            int limit = p.seq - kv0;
-            if (p.causal) limit = min(limit, q_row - kv0 + 1);
-            const bool need_mask = __any_sync(0xffffffffu, limit < kBlockKV);
-            // Scores in log2 units are s * c. For c > 0 the max of the raw scores is
-            // scaled once and each exponent argument is a single FMA; otherwise the
-            // scores are scaled first. Masking runs only for blocks where some row
-            // of the warp has a masked key (the choice is warp-uniform).
-            const float c_in = p.scale_log2;
-            const bool pos_scale = c_in > 0.0f;
-            const float c_eff = pos_scale ? c_in : 1.0f;
-            const bool fast = pos_scale && !need_mask;
-            float m_use, alpha, e_sum;
-            if (pos_scale && !single) {
-                // Whole row in registers. Masked keys (causal diagonal, sequence
-                // tail) become -inf in place, so their exponentials are exactly 0.
-                uint32_t r[128];
-                load_row128(s_addr, r);
-                if (need_mask) mask_row128(r, limit);
-                next_point(m_run, row_max128(r) * c_eff, m_use, alpha);
-                e_sum = row_exp_store128(s_addr, r, c_eff, -m_use);
-            } else {
-                const float m_raw = fast ? score_row_max<true>(s_addr, limit, pos_scale, c_in)
-                                         : score_row_max<false>(s_addr, limit, pos_scale, c_in);
-                next_point(m_run, m_raw * c_eff, m_use, alpha);
-                const float neg_m = -m_use;
-                if (single) {
-                    // One key block holds the whole row: sum first, then normalise and
-                    // round (the exponentials are recomputed from the intact S).
-                    e_sum = fast ? score_row_exp<true, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f)
-                                 : score_row_exp<false, 1>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
-                    if (fast) {
-                        score_row_exp<true, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
-                    } else {
-                        score_row_exp<false, 2>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, e_sum);
-                    }
-                } else {
-                    e_sum = score_row_exp<false, 0>(s_addr, limit, pos_scale, c_in, c_eff, neg_m, 1.0f);
-                }
-            }
-            // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp
-            // when any of its rows needs it (alpha == 1 rows multiply by one).
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                // Rescale the running output: PV_{j-1} has completed (in-order tcgen05).
-#pragma unroll
-                for (int c = 0; c < kDPad / 16; ++c) {
-                    uint32_t r[16];
-                    tmem_ld_32x32b_x16(o_addr + 16 * c, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-                    tmem_st_32x32b_x16(o_addr + 16 * c, r);
-                }
-            }
-            l_run = l_run * alpha + e_sum;
-            m_run = m_use;
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_ready(g));
-        }
-        if (ok && mbar_wait_warp(o_final(g), 0, kFaultAttnWait, abort_flag)) {
+            of_phase ^= 1u;
             tc_fence_after();
             const bool row_ok = q_row < p.seq;
-            float* orow = p.out + (static_cast<long long>(bh) * p.seq + q_row) * p.head_dim;
+            // Multiple rounding: one reciprocal of the row sum, then products (within
+            // 2^-23 relative of a division, far inside the error bound).
+            const float inv_l = single ? 1.0f : __frcp_rn(l_run);
+            float* orow = p.out + (static_cast<long long>(it.bh) * p.seq + q_row) * p.head_dim;
 #pragma unroll
             for (int c = 0; c < kDPad / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(o_addr + 32 * c, r);
                 tmem_wait_ld();
+                if (c == kDPad / 32 - 1) {
+                    // O_g is in registers: the next item's first PV may overwrite it.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(o_empty(g));
+                }
                 if (row_ok) {
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         const int col = 32 * c + 4 * q;
                         if (col < p.head_dim) {
                             float4 v;
-                            v.x = __uint_as_float(r[4 * q]);
-                            v.y = __uint_as_float(r[4 * q + 1]);
-                            v.z = __uint_as_float(r[4 * q + 2]);
-                            v.w = __uint_as_float(r[4 * q + 3]);
-                            if (!single) {
-                                v.x = __fdiv_rn(v.x, l_run);
-                                v.y = __fdiv_rn(v.y, l_run);
-                                v.z = __fdiv_rn(v.z, l_run);
-                                v.w = __fdiv_rn(v.w, l_run);
-                            }
+                            v.x = __uint_as_float(r[4 * q]) * inv_l;
+                            v.y = __uint_as_float(r[4 * q + 1]) * inv_l;
+                            v.z = __uint_as_float(r[4 * q + 2]) * inv_l;
+                            v.w = __uint_as_float(r[4 * q + 3]) * inv_l;
                             if (p.out_vec4) {
                                 __stcs(reinterpret_cast<float4*>(orow + col), v);
                             } else {
@@ -657,7 +765,7 @@ __global__ void repack_kernel(const uint16_t* src, uint16_t* dst, long long coun
 }
 
 template <int kDPad>
-cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, int device,
+cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, int device, int grid,
                    cudaStream_t stream) {
     using Cc = Cfg<kDPad>;
     static bool configured[host::kMaxDevices] = {};
@@ -681,7 +789,6 @@ cudaError_t launch(const void* q, const void* k, const void* v, const Params& p,
         !host::make_map_f16(&mv, v, 3, dims_kv, strides, box)) {
         return cudaErrorInvalidValue;
     }
-    const long long grid = static_cast<long long>(p.bh) * p.pairs;
     kernel<<<static_cast<unsigned>(grid), kThreads, Cc::kSmemBytes, stream>>>(mq, mk, mv, p);
     return cudaSuccess;
 }
@@ -707,8 +814,8 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
             return cudaErrorInvalidValue;
         }
     }
-    int device = 0;
-    cudaError_t err = host::current_device(&device, nullptr);
+    int device = 0, sm_count = 0;
+    cudaError_t err = host::current_device(&device, &sm_count);
     if (err != cudaSuccess) return err;
     static_cast<void>(cudaGetLastError());
 
@@ -732,6 +839,12 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
     p.causal = causal;
     p.out = out;
     p.out_vec4 = (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    p.num_items = p.bh * p.pairs;
+    p.next_item = nullptr;
+    // One resident CTA per SM (shared memory and all 512 TMEM columns). With more
+    // items than SMs, the CTAs take further items from a counter in stream-ordered
+    // scratch memory, zeroed before the launch.
+    const int grid = p.num_items < sm_count ? p.num_items : sm_count;
 
     // TMA needs 16-byte aligned bases; copy misaligned operands first.
     const size_t elems_q = static_cast<size_t>(p.bh) * static_cast<size_t>(seq) * head_dim;
@@ -749,10 +862,17 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
             src[i] = tmp[i];
         }
     }
-    if (err == cudaSuccess) {
-        err = head_dim == 128 ? launch<128>(src[0], src[1], src[2], p, device, stream)
-                              : launch<64>(src[0], src[1], src[2], p, device, stream);
+    void* counter = nullptr;
+    if (err == cudaSuccess && p.num_items > grid) {
+        err = host::scratch_alloc(&counter, sizeof(int), device, stream);
+        if (err == cudaSuccess) err = cudaMemsetAsync(counter, 0, sizeof(int), stream);
+        p.next_item = static_cast<int*>(counter);
     }
+    if (err == cudaSuccess) {
+        err = head_dim == 128 ? launch<128>(src[0], src[1], src[2], p, device, grid, stream)
+                              : launch<64>(src[0], src[1], src[2], p, device, grid, stream);
+    }
+    if (counter != nullptr) cudaFreeAsync(counter, stream);
     for (int i = 0; i < 3; ++i)
         if (tmp[i] != nullptr) cudaFreeAsync(tmp[i], stream);
     if (err != cudaSuccess) return err;
