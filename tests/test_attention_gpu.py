@@ -160,3 +160,53 @@ def test_more_items_than_sms_every_head(causal):
     so the persistent CTAs take items from the shared counter and run several items
     each; every output row of every head is checked."""
     general_case(1, 300, 256, 64, causal, seed=7)
+
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1, 128), (2, 3, 128, 128), (1, 2, 129, 128), (1, 1, 300, 128),
+                                   (2, 1, 1000, 128), (1, 2, 517, 128)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("causal", [False, True])
+def test_head128_shapes(shape, causal):
+    """head_dim 128 on single-block, tail and multi-block shapes."""
+    b, h, s, d = shape
+    general_case(b, h, s, d, causal, seed=11 + sum(shape))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_head128_many_items_gqa_and_misaligned(causal):
+    """More items than SMs (dynamic scheduling), grouped-query heads and misaligned
+    operands at head_dim 128."""
+    general_case(1, 160, 512, 128, causal, seed=21)
+    general_case(1, 1, 200, 128, causal, seed=22, misaligned=True)
+    b, heads_q, heads_kv, s, d = 2, 6, 2, 257, 128
+    group = heads_q // heads_kv
+    q, _, _ = oracle.gen_qkv_normal(61, 1.0, b * heads_q * s * d)
+    _, k, v = oracle.gen_qkv_normal(62, 1.0, b * heads_kv * s * d)
+    out = torch.full((b * heads_q * s * d,), float("nan"), device="cuda")
+    tq, tk_, tv = dev(q), dev(k), dev(v)
+    assert tk_b200.attention_gqa_raw(tq, tk_, tv, out, b, heads_q, heads_kv, s, d, 1 / math.sqrt(d), causal) == 0
+    got = host(out).reshape(b * heads_q, s, d)
+    qs = q.reshape(b * heads_q, s, d)
+    ks, vs = k.reshape(b * heads_kv, s, d), v.reshape(b * heads_kv, s, d)
+    for bh in range(b * heads_q):
+        kv = (bh // heads_q) * heads_kv + (bh % heads_q) // group
+        want = oracle.attention_ref(qs[bh], ks[kv], vs[kv], s, d, 1 / math.sqrt(d), causal)
+        bound = oracle.attention_bound(vs[kv], s, d)
+        assert np.all(np.abs(got[bh] - want) <= bound[None, :]), bh
+
+
+@pytest.mark.parametrize("scale", [-0.3, 0.0])
+def test_non_positive_scale(scale):
+    """A negative or zero scale (scores are scaled before the max; masked keys stay -inf)."""
+    b, h, s, d = 1, 2, 300, 128
+    q, k, v = oracle.gen_qkv_normal(31, 1.0, b * h * s * d)
+    out = torch.full((b * h * s * d,), float("nan"), device="cuda")
+    tq, tk_, tv = dev(q), dev(k), dev(v)
+    for causal in (False, True):
+        assert tk_b200.attention_raw(tq, tk_, tv, out, b, h, s, d, scale, causal) == 0
+        got = host(out).reshape(b * h, s, d)
+        for bh in range(b * h):
+            sl = slice(bh * s * d, (bh + 1) * s * d)
+            want = oracle.attention_ref(q[sl], k[sl], v[sl], s, d, scale, causal)
+            bound = oracle.attention_bound(v[sl], s, d)
+            assert np.all(np.abs(got[bh] - want) <= bound[None, :]), (causal, bh)
