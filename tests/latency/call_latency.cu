@@ -3,6 +3,7 @@
 // overhead enters the numbers:
 //   * GEMM (bench/gemm_throughput.cu:94-120): two warm-up calls, then five calls
 //     each bracketed by CUDA events on the default stream; the best one counts.
+//     Square sizes 256..4096 and the decode shape 16 x 4096 x 4096.
 //   * one-tile attention (bench/attention_throughput.cu:128-165, 206-233): 2048
 //     back-to-back calls between two events, four rounds alternating unmasked and
 //     causal, the median round in microseconds per public call.
@@ -53,12 +54,12 @@ double since_us(Clock::time_point t0) {
     return std::chrono::duration<double, std::micro>(Clock::now() - t0).count();
 }
 
-// Best single-call time of an m = n = k = size GEMM, in microseconds, and the
-// smallest host time spent inside the call.
-bool gemm_best_us(const Impl& impl, int size, const __half* a, const __half* b, float* c, double* us,
+// Best single-call time of an m x n x k GEMM (dense leading dimensions), in
+// microseconds, and the smallest host time spent inside the call.
+bool gemm_best_us(const Impl& impl, int m, int n, int k, const __half* a, const __half* b, float* c, double* us,
                   double* host_us) {
     for (int i = 0; i < 2; ++i)
-        if (!check(impl.gemm(size, size, size, a, size, b, size, c, size, nullptr), "gemm warm-up")) return false;
+        if (!check(impl.gemm(m, n, k, a, k, b, n, c, n, nullptr), "gemm warm-up")) return false;
     if (!check(cudaDeviceSynchronize(), "synchronize")) return false;
     cudaEvent_t start, stop;
     cudaEventCreate(&start);
@@ -69,7 +70,7 @@ bool gemm_best_us(const Impl& impl, int size, const __half* a, const __half* b, 
     for (int i = 0; i < 5 && ok; ++i) {
         ok = check(cudaEventRecord(start), "record");
         const Clock::time_point t0 = Clock::now();
-        ok = ok && check(impl.gemm(size, size, size, a, size, b, size, c, size, nullptr), "gemm");
+        ok = ok && check(impl.gemm(m, n, k, a, k, b, n, c, n, nullptr), "gemm");
         *host_us = std::min(*host_us, since_us(t0));
         ok = ok && check(cudaEventRecord(stop), "record") && check(cudaEventSynchronize(stop), "sync");
         float ms = 0.0f;
@@ -140,9 +141,16 @@ int main(int argc, char** argv) {
     for (const Impl& impl : impls) {
         for (int size : sizes) {
             double us = 0, host_us = 0;
-            if (!gemm_best_us(impl, size, a, b, c, &us, &host_us)) return 1;
+            if (!gemm_best_us(impl, size, size, size, a, b, c, &us, &host_us)) return 1;
             std::printf("{\"impl\": \"%s\", \"call\": \"gemm_%d\", \"us\": %.3f, \"host_us\": %.3f}\n", impl.name,
                         size, us, host_us);
+        }
+        {
+            // The decode-shaped configuration, 16 x 4096 x 4096.
+            double us = 0, host_us = 0;
+            if (!gemm_best_us(impl, 16, 4096, 4096, a, b, c, &us, &host_us)) return 1;
+            std::printf("{\"impl\": \"%s\", \"call\": \"gemm_16x4096x4096\", \"us\": %.3f, \"host_us\": %.3f}\n",
+                        impl.name, us, host_us);
         }
         double rounds[2][4], host[2][4];
         for (int round = 0; round < 4; ++round)

@@ -164,6 +164,25 @@ def test_decode_16x4096x4096():
     assert oracle.gemm_check(k, c, r, s, n, n)[0] == 0
 
 
+@pytest.mark.parametrize("m,n,k,ldc,cta_group", [(48, 784, 2048, 787, 0), (304, 512, 4096, 512, 1),
+                                                 (304, 512, 4096, 520, 2), (16, 4096, 4096, 4096, 0)],
+                         ids=["ragged_n_scalar_c", "pairs_off", "cta_pairs", "decode"])
+def test_split_k_in_kernel_reduction(m, n, k, ldc, cta_group):
+    """Split-K shapes (few output tiles, long K): the CTA that completes a tile's
+    last split sums the partials in split order. Results within the error bound,
+    C padding untouched, and bit-identical across two runs (the order does not
+    depend on which CTA finishes last)."""
+    a, b = oracle.gen_gemm_normal(5, 0.02, m, n, k, k, n)
+    sentinel = np.float32(-7.0)
+    c1 = run_gemm(m, n, k, a, k, b, n, ldc, sentinel=sentinel, cta_group=cta_group)
+    c2 = run_gemm(m, n, k, a, k, b, n, ldc, sentinel=sentinel, cta_group=cta_group)
+    assert np.array_equal(c1.view(np.uint32), c2.view(np.uint32))
+    assert np.all(c1[:, n:] == sentinel)
+    r, s = oracle.gemm_ref(m, n, k, a, k, b, n)
+    assert oracle.gemm_check(k, np.ascontiguousarray(c1[:, :n]), r, s, n, n)[0] == 0
+    assert tk_b200.device_status() == 0
+
+
 def test_error_state_contract():
     rt = cudart()
     a = torch.zeros((16, 16), dtype=torch.float16, device="cuda")

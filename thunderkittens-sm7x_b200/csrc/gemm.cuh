@@ -60,7 +60,7 @@ struct Params {
     int num_tiles;      // m_tiles * n_tiles * k_splits work units
     // Split-K (small-M problems): unit t covers K blocks [ks * kb_per_split, ...)
     // and writes its partial C to ws[ks][m][n] (dense); splitk_reduce_kernel then
-    // sums the splits in order into C. k_splits == 1 writes C directly.
+    // sums the splits in order into C (deterministic). k_splits == 1 writes C directly.
     int k_splits, kb_per_split;
     float* ws;
     // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kCtaGroup == 2) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // A programmatic dependent (the split-K reduction) may be scheduled now; it
+    // waits for this grid's completion before reading anything.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 4) {
         // ---------------- producer ----------------
@@ -474,8 +477,12 @@ __global__ void __launch_bounds__(256) rowsoftmax_apply_kernel(const float2* par
 }
 
 // Sums the split-K partials ws[0..splits)[m][n] in split order into C (ldc).
+// Launched as a programmatic dependent of the GEMM: it may start while the GEMM's
+// last CTAs finish, and griddepcontrol.wait holds it until the GEMM has completed
+// and its partials are visible.
 __global__ void splitk_reduce_kernel(const float* ws, int splits, int m, int n, float* c, long long ldc,
                                      bool c_vec4) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const long long quads = static_cast<long long>(m) * (n / 4);
     const long long plane = static_cast<long long>(m) * n;
     for (long long q = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; q < quads;

@@ -298,7 +298,18 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         if (err == cudaSuccess) {
             const long long quads = static_cast<long long>(m) * (n / 4);
             const int blocks = static_cast<int>(quads / 256 + 1 < 4 * sm_count ? quads / 256 + 1 : 4 * sm_count);
-            tk::gemm::splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p.ws, p.k_splits, m, n, c, ldc, p.c_vec4);
+            // Programmatic dependent launch: the reduction's launch overlaps the GEMM's tail.
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+            cfg.blockDim = dim3(256);
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            err = cudaLaunchKernelEx(&cfg, tk::gemm::splitk_reduce_kernel, static_cast<const float*>(p.ws), p.k_splits,
+                                     m, n, c, static_cast<long long>(ldc), p.c_vec4);
         }
         cudaFreeAsync(p.ws, stream);
     }
