@@ -25,7 +25,7 @@ namespace rowops {
 enum : int { kSum = 1, kMax = 2, kSoftmax = 4, kCausal = 8 };
 
 constexpr int kThreads = 256;            // 8 warps per block
-constexpr int kTilesPerWarpStep = 2;     // tiles in flight per warp step
+constexpr int kTilesPerWarpStep = 8;     // tiles in flight per warp step (16 KiB of loads per warp)
 
 // The tree, max-tie rule and softmax are the public device-level tile API
 // (include/tk_sm7x/tile_b200.cuh), whose tile16 layout is exactly the layout of a
