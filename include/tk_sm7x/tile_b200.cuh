@@ -137,6 +137,25 @@ __device__ __forceinline__ void store(float* dst, int ld, const tile16& t) {
     }
 }
 
+// Element-wise in registers: the counterparts of tk_sm7x::zero / tk_sm7x::scale
+// (include/tk_sm7x/tile.cuh:126-153). Scaling is one FP32 multiply per element,
+// exact for power-of-two factors in the normal range.
+__device__ __forceinline__ void zero(tile16& t) {
+    t.lo = make_float4(0.f, 0.f, 0.f, 0.f);
+    t.hi = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+__device__ __forceinline__ void scale(tile16& t, float factor) {
+    t.lo.x *= factor;
+    t.lo.y *= factor;
+    t.lo.z *= factor;
+    t.lo.w *= factor;
+    t.hi.x *= factor;
+    t.hi.y *= factor;
+    t.hi.z *= factor;
+    t.hi.w *= factor;
+}
+
 // Row sums / maxima in registers: .x is the lane's row lane/4, .y row 8 + lane/4.
 __device__ __forceinline__ float2 row_sum(const tile16& t) {
     return make_float2(quad_reduce<op_sum>(t.lo.x, t.lo.y, t.lo.z, t.lo.w),

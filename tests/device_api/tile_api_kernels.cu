@@ -47,3 +47,17 @@ extern "C" int tile_api_run(const float* in, int ld, int n_tiles, float* sums, f
     if (cudaGetLastError() != cudaSuccess) return 1;
     return cudaDeviceSynchronize() == cudaSuccess ? 0 : 2;
 }
+
+// tk_sm7x::scale's counterpart: load a tile, scale it in registers, store it.
+__global__ void tile_scale_kernel(const float* in, float* out, float factor) {
+    b200::tile16 tile;
+    b200::load(tile, in, 16);
+    b200::scale(tile, factor);
+    b200::store(out, 16, tile);
+}
+
+extern "C" int tile_scale_run(const float* in, float* out, float factor) {
+    tile_scale_kernel<<<1, 32>>>(in, out, factor);
+    if (cudaGetLastError() != cudaSuccess) return 1;
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : 2;
+}

@@ -30,6 +30,8 @@ def tile_api(tmp_path_factory):
     lib = C.CDLL(str(so))
     lib.tile_api_run.restype = C.c_int
     lib.tile_api_run.argtypes = [C.c_void_p, C.c_int, C.c_int] + [C.c_void_p] * 7
+    lib.tile_scale_run.restype = C.c_int
+    lib.tile_scale_run.argtypes = [C.c_void_p, C.c_void_p, C.c_float]
     return lib
 
 
@@ -104,3 +106,23 @@ def test_example_gemm_row_softmax(tile_api):
     assert np.all((got >= 0) & (got <= 1))
     assert np.max(np.abs(got - want)) <= oracle.SOFTMAX_BOUND
     assert np.all(np.abs(got.sum(axis=1) - 1.0) <= oracle.SOFTMAX_BOUND)
+
+
+@pytest.mark.parametrize("factor", [0.25, -0.5])
+def test_tile_scale_exact(tile_api, factor):
+    """tests/tile_scale.cu:47-63: C = A B with A = diag((i + 1) / 16) and
+    B[i][j] = (16 i + j - 128) / 8 (the library GEMM, exact for these values), then
+    the tile scaled by a power of two in registers: every element exactly
+    factor * (i + 1) / 16 * (16 i + j - 128) / 8."""
+    i = np.arange(16)[:, None].astype(np.float32)
+    j = np.arange(16)[None, :].astype(np.float32)
+    a = np.where(i == j, (i + 1) / 16, 0).astype(np.float32)
+    b = ((16 * i + j - 128) / 8).astype(np.float32)
+    da = torch.from_numpy(a).half().cuda()
+    db = torch.from_numpy(b).half().cuda()
+    c = tk_b200.gemm(da, db)
+    out = torch.full((256,), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    assert tile_api.tile_scale_run(c.data_ptr(), out.data_ptr(), factor) == 0
+    want = (np.float32(factor) * ((i + 1) / 16) * ((16 * i + j - 128) / 8)).astype(np.float32)
+    assert np.array_equal(bits(host(out).reshape(16, 16)), bits(want))
