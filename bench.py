@@ -164,7 +164,7 @@ def max_over_ranks(value: float, world: int) -> float:
 class Workload:
     """Device-resident inputs and the list of (name, launch, flops_or_bytes) calls of one step."""
 
-    def __init__(self, kind: str, rank: int, world: int, row_tiles: int = ROW_TILES):
+    def __init__(self, kind: str, rank: int, world: int, row_tiles: int = ROW_TILES, fused_gather: bool = False):
         import torch
         import tk_b200
         self.kind = kind
@@ -173,14 +173,27 @@ class Workload:
         self.calls = []
         self.h2d = []   # (device tensor) inputs copied in per e2e step
         self.d2h = []   # (device tensor) outputs copied out per e2e step
+        self.gathered = []  # outputs already gathered by their kernel (fused all-gather)
+        self.gbuf = None
         if kind in ("headline", "gemm"):
             gen.manual_seed(2 + 1000 * rank)
             self.a = (torch.rand(GEMM_M, GEMM_K, device="cuda", generator=gen) * 2 - 1).half()
             gen.manual_seed(2)
             self.b = (torch.rand(GEMM_K, GEMM_N, device="cuda", generator=gen) * 2 - 1).half()
-            self.c = torch.empty(GEMM_M, GEMM_N, device="cuda")
-            self.calls.append(("gemm_8192", lambda: self.tk.gemm_raw(
-                GEMM_M, GEMM_N, GEMM_K, self.a, GEMM_K, self.b, GEMM_N, self.c, GEMM_N), gemm_flops(), 1))
+            if fused_gather and world > 1:
+                # Every rank's 8192-row block lands in every rank's gathered C from the
+                # GEMM epilogue (NVLink stores), no separate collective.
+                from tk_b200 import dist as tkd
+                self.gbuf = tkd.GatheredBuffer(world * GEMM_M, GEMM_N)
+                self.c = self.gbuf.tensor()[rank * GEMM_M:(rank + 1) * GEMM_M]
+                self.calls.append(("gemm_8192", lambda: self.tk.gemm_gather_raw(
+                    GEMM_M, GEMM_N, GEMM_K, self.a, GEMM_K, self.b, GEMM_N, self.gbuf.ptrs, rank, GEMM_N),
+                    gemm_flops(), 1))
+                self.gathered.append(self.c)
+            else:
+                self.c = torch.empty(GEMM_M, GEMM_N, device="cuda")
+                self.calls.append(("gemm_8192", lambda: self.tk.gemm_raw(
+                    GEMM_M, GEMM_N, GEMM_K, self.a, GEMM_K, self.b, GEMM_N, self.c, GEMM_N), gemm_flops(), 1))
             self.h2d += [self.a, self.b]
             self.d2h += [self.c]
         if kind in ("headline", "attention"):
@@ -224,7 +237,8 @@ class Workload:
 
 def run_ours(args, rank, world, local):
     import torch
-    wl = Workload(args.workload, rank, world, args.row_tiles)
+    fused = args.gather == "fused"
+    wl = Workload(args.workload, rank, world, args.row_tiles, fused_gather=fused)
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -261,7 +275,7 @@ def run_ours(args, rank, world, local):
     # device buffer sets and separate copy streams let step i's kernels overlap the
     # host->device copy of step i+1 and the device->host copy of step i-1 (the PCIe
     # directions are independent), as a pipelined host application would run.
-    wl2 = Workload(args.workload, rank, world, args.row_tiles)
+    wl2 = Workload(args.workload, rank, world, args.row_tiles, fused_gather=fused)
     sets = [wl, wl2]
     # One pinned host copy of the inputs and one of the outputs serve both device
     # sets: copies in one direction are serialised on their stream.
@@ -315,6 +329,8 @@ def run_ours(args, rank, world, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
     h2d_bytes = sum(t.numel() * t.element_size() for t in wl.h2d)
     d2h_bytes = sum(t.numel() * t.element_size() for t in wl.d2h)
+    if wl2.gbuf is not None:
+        wl2.gbuf.close()  # collective
     del wl2, host_in, host_out, host_in_set, host_out_set
 
     status = wl.tk.device_status()
@@ -324,10 +340,13 @@ def run_ours(args, rank, world, local):
 
 
 def gather_outputs(wl, world):
-    """NCCL all-gather of this step's outputs (only with --gather)."""
+    """NCCL all-gather of this step's outputs not already gathered by their kernel
+    (only with --gather)."""
     import torch
     import torch.distributed as dist
     for t in wl.d2h:
+        if any(t is g for g in wl.gathered):
+            continue
         out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
         dist.all_gather_into_tensor(out, t)
 
@@ -479,7 +498,7 @@ def main_ours(args):
                                    "per GPU"}[args.workload],
             "parallelism": f"dp{world} (GEMM by M row blocks, attention by batch x head, row ops by tile range)",
             "l2": "inputs larger than L2 (126 MB): no flush needed",
-            "gather": bool(args.gather),
+            "gather": args.gather or False,
         }
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
@@ -494,6 +513,8 @@ def main_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        if wl.gbuf is not None:
+            wl.gbuf.close()  # collective
         dist.destroy_process_group()
 
 
@@ -567,7 +588,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["headline", "gemm", "attention", "rowops"], default="headline")
-    ap.add_argument("--gather", action="store_true", help="NCCL all-gather of each step's outputs")
+    ap.add_argument("--gather", nargs="?", const="fused", default=None, choices=["fused", "nccl"],
+                    help="gather each step's outputs on every rank: 'fused' (default) stores the GEMM's C "
+                         "into every rank's buffer from the GEMM epilogue and all-gathers the attention "
+                         "outputs with NCCL; 'nccl' all-gathers every output with NCCL after its kernel")
     ap.add_argument("--row-tiles", type=int, default=ROW_TILES,
                     help="tiles per GPU of the rowops workload (default 1,048,576; inputs stay larger than L2 "
                          "above 126,000)")

@@ -117,6 +117,31 @@ TK_API cudaError_t tk_gemm_f16_f16_f32_nn_rowsoftmax(int m, int n, int k, const 
                                                      float* c, int ldc, float* probs, int ldp,
                                                      cudaStream_t stream);
 
+/* Multi-GPU GEMM with the all-gather fused into the epilogue (no counterpart in
+ * the reference, which has no multi-GPU code). Rank `rank` of `n_ranks`
+ * (1 <= n_ranks <= 8) computes its m rows of C = A B and stores them, tile by
+ * tile as the MMAs finish, at rows [rank * m, rank * m + m) of every rank's
+ * gathered buffer c_ranks[0 .. n_ranks) (n_ranks * m rows, leading dimension
+ * ldc): c_ranks[rank] is this rank's own buffer, the others are the peers'
+ * buffers mapped into this process (tk_ipc_open), written over NVLink with plain
+ * stores. A, B and the argument rules are those of tk_gemm_f16_f16_f32_nn. Rank r
+ * may read its buffer once every rank's call has completed (the caller
+ * synchronises its stream and then the ranks, e.g. with a host barrier). */
+TK_API cudaError_t tk_gemm_f16_f16_f32_nn_gather(int m, int n, int k, const void* a, int lda,
+                                                 const void* b, int ldb, float* const* c_ranks,
+                                                 int n_ranks, int rank, int ldc,
+                                                 cudaStream_t stream);
+
+/* Device memory that other processes can map (for the gathered GEMM's buffers;
+ * no counterpart in the reference). tk_ipc_alloc: cudaMalloc of `bytes` on the
+ * current device and its cudaIpcMemHandle_t (64 bytes) in `handle`;
+ * tk_ipc_open: maps a handle from another process (peer access enabled);
+ * tk_ipc_close unmaps it; tk_ipc_free frees an allocation of tk_ipc_alloc. */
+TK_API cudaError_t tk_ipc_alloc(size_t bytes, void** ptr, void* handle);
+TK_API cudaError_t tk_ipc_open(const void* handle, void** ptr);
+TK_API cudaError_t tk_ipc_close(void* ptr);
+TK_API cudaError_t tk_ipc_free(void* ptr);
+
 /* Tuning knob, no counterpart in the reference (whose tile choice is the fixed
  * rule of src/gemm.cu:50-57): 0 = choose by problem size (default), 1 = one CTA
  * per 128 x 256 tile, 2 = CTA pairs on 256 x 256 tiles. Process-wide; returns

@@ -200,3 +200,48 @@ def test_error_state_contract():
     torch.cuda.synchronize()
     assert torch.all(c == 0.0)
     assert tk_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k,ldc,cta_group", [(512, 1024, 2048, 1024, 0), (256, 784, 512, 790, 1),
+                                                 (768, 512, 1024, 520, 2)],
+                         ids=["vec", "scalar_ldc", "cta_pairs"])
+def test_gather_epilogue_two_local_buffers(m, n, k, ldc, cta_group):
+    """tk_gemm_f16_f16_f32_nn_gather on one GPU with two local buffers standing in for
+    two ranks: the call for rank r stores its m rows at rows [r m, r m + m) of both
+    buffers. Every block within the error bound, padding and the other rank's rows
+    untouched by a call, and the two buffers bit-identical."""
+    blocks = [oracle.gen_gemm_normal(100 + r, 0.02, m, n, k, k, n) for r in range(2)]
+    b = blocks[0][1]
+    sentinel = np.float32(-3.0)
+    bufs = [torch.full((2 * m, ldc), float(sentinel), device="cuda") for _ in range(2)]
+    ptrs = [t.data_ptr() for t in bufs]
+    db = dev(b)
+    prev = tk_b200.set_gemm_cta_group(cta_group)
+    try:
+        for r in range(2):
+            assert tk_b200.gemm_gather_raw(m, n, k, dev(blocks[r][0]), k, db, n, ptrs, r, ldc) == 0
+            if r == 0:
+                first = host(bufs[0])
+                assert np.all(first[m:] == sentinel)  # rank 1's rows not written by rank 0's call
+    finally:
+        tk_b200.set_gemm_cta_group(prev)
+    got = [host(t) for t in bufs]
+    assert np.array_equal(got[0].view(np.uint32), got[1].view(np.uint32))
+    assert np.all(got[0][:, n:] == sentinel)
+    for r in range(2):
+        ref, sabs = oracle.gemm_ref(m, n, k, blocks[r][0], k, b, n)
+        part = np.ascontiguousarray(got[0][r * m:(r + 1) * m, :n])
+        assert oracle.gemm_check(k, part, ref, sabs, n, n)[0] == 0
+    assert tk_b200.device_status() == 0
+
+
+def test_gather_invalid_arguments():
+    a = torch.zeros((16, 16), dtype=torch.float16, device="cuda")
+    c = torch.zeros((32, 16), device="cuda")
+    p = [c.data_ptr(), c.data_ptr()]
+    bad = tk_b200.CUDA_ERROR_INVALID_VALUE
+    assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p, 2, 16) == bad   # rank out of range
+    assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p[:1] * 9, 0, 16) == bad  # more than 8 ranks
+    assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, [c.data_ptr(), 0], 0, 16) == bad  # null buffer
+    assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p, 0, 8) == bad   # ldc < n
+    assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p, 1, 16) == 0

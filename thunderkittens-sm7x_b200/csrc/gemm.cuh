@@ -37,6 +37,7 @@ constexpr int kMmaK = 16;      // K per tcgen05.mma (kind::f16)
 constexpr int kGroupM = 16;    // tile-rows per rasterisation group
 constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
 constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
+constexpr int kMaxGatherRanks = 8;   // destinations of the all-gather epilogue
 
 template <int kCtaGroup>
 struct Cfg {
@@ -47,7 +48,10 @@ struct Cfg {
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = kCtaGroup == 1 ? 4 : 6;
     static constexpr int kBarrierBytes = 256;
-    static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;  // + align slack
+    // kEpiGather: a 32 x 33-float transpose buffer per epilogue warp, so that the
+    // stores into the ranks' buffers are whole 128-byte row segments.
+    static constexpr int kXposeBytes = 4 * 32 * 33 * 4;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + kXposeBytes + 1024;  // + align slack
     static constexpr uint32_t kIdesc = idesc_f16_f32(kBlockM * kCtaGroup, kBlockN, 0, 1);
 };
 
@@ -65,6 +69,12 @@ struct Params {
     float* ws;
     // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
     float* partial;     // [m][n_tiles][2] (max, sum), or null
+    // kEpiGather: row r of this GEMM goes to row dst_row0 + r of every dst[0..n_dst)
+    // (this rank's gathered buffer and the peers' buffers mapped into this process),
+    // leading dimension ldc, so the all-gather's transfer overlaps the MMAs tile by tile.
+    float* dst[kMaxGatherRanks];
+    int n_dst;
+    long long dst_row0;
 };
 
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int* tm, int* tn) {
@@ -111,6 +121,7 @@ enum Stats : int {
     kStatsNone = 0,
     kStatsMaxSum = 1,   // (row max, row sum) of the tile's columns, fixed pairwise order
     kStatsSoftmax = 2,  // (row max m_t, sum of exp(c - m_t)) for a full-row softmax
+    kEpiGather = 3,     // no statistics; each row stored to every Params::dst (multi-GPU all-gather)
 };
 
 template <int kCtaGroup, int kStats>
@@ -308,23 +319,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_32x32b_x32(t_addr + chunk * 32, r);
                 tmem_wait_ld();
                 const int col0 = col_base + chunk * 32;
-                if (row_ok) {
-                    if (vec4) {
+                if constexpr (kStats == kEpiGather) {
+                    // Through shared memory: lane l holds row (32 warp + l) of the chunk;
+                    // after the transpose, one store instruction writes one row's 32
+                    // consecutive columns (128 bytes) into every destination.
+                    float* xp = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes + C::kBarrierBytes) +
+                                warp * (32 * 33);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            if (col0 + q * 4 < p.n) {
-                                float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-                                *reinterpret_cast<float4*>(crow + col0 + q * 4) = v;
+                    for (int q = 0; q < 32; ++q) xp[lane * 33 + q] = __uint_as_float(r[q]);
+                    __syncwarp();
+                    const long long row_first = static_cast<long long>(tm) * C::kTileM + rank * kBlockM + warp * 32;
+                    const bool col_ok = col0 + static_cast<int>(lane) < p.n;
+                    for (int i = 0; i < 32; ++i) {
+                        const long long rr = row_first + i;
+                        if (rr >= p.m) break;  // warp-uniform
+                        const float v = xp[i * 33 + lane];
+                        if (col_ok) {
+#pragma unroll
+                            for (int d = 0; d < kMaxGatherRanks; ++d) {
+                                if (d >= p.n_dst) break;
+                                p.dst[d][(p.dst_row0 + rr) * p.ldc + col0 + lane] = v;
                             }
                         }
-                    } else {
+                    }
+                    __syncwarp();
+                }
+                constexpr int kDsts = kStats == kEpiGather ? 0 : 1;
 #pragma unroll
-                        for (int q = 0; q < 32; ++q)
-                            if (col0 + q < p.n) crow[col0 + q] = __uint_as_float(r[q]);
+                for (int d = 0; d < kDsts; ++d) {
+                    float* const drow = crow;
+                    if (row_ok) {
+                        if (vec4) {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                if (col0 + q * 4 < p.n) {
+                                    float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                           __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                                    *reinterpret_cast<float4*>(drow + col0 + q * 4) = v;
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 32; ++q)
+                                if (col0 + q < p.n) drow[col0 + q] = __uint_as_float(r[q]);
+                        }
                     }
                 }
-                if constexpr (kStats != kStatsNone) {
+                if constexpr (kStats == kStatsMaxSum || kStats == kStatsSoftmax) {
                     float x[32];
 #pragma unroll
                     for (int q = 0; q < 32; ++q) x[q] = __uint_as_float(r[q]);

@@ -9,6 +9,7 @@
 
 #include <climits>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "attention.cuh"
@@ -144,10 +145,20 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
 }
 
+// Destinations of the multi-GPU gathered GEMM: rank `rank` of `count` writes its m
+// rows at row rank * m of each buffer (count == 0: an ordinary GEMM into c).
+struct Gather {
+    float* const* bufs = nullptr;
+    int count = 0;
+    int rank = 0;
+};
+
 cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b, int ldb, float* c,
-                      int ldc, float* row_max, float* row_sum, float* probs, int ldp, cudaStream_t stream) {
+                      int ldc, float* row_max, float* row_sum, float* probs, int ldp, cudaStream_t stream,
+                      Gather gather = Gather{}) {
     const bool softmax = probs != nullptr;
     const bool stats = row_max != nullptr || row_sum != nullptr || softmax;
+    const bool gathered = gather.count > 0;
     if (a == nullptr || b == nullptr || c == nullptr || m <= 0 || n <= 0 || k <= 0 || m % 16 != 0 ||
         n % 16 != 0 || k % 16 != 0 || lda < k || ldb < n || ldc < n) {
         return cudaErrorInvalidValue;
@@ -164,6 +175,11 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         (row_max == nullptr || row_sum == nullptr ||
          tk::host::ranges_overlap(row_max, sizeof(float) * m, row_sum, sizeof(float) * m))) {
         return cudaErrorInvalidValue;
+    }
+    bool gather_vec4 = true;
+    if (gathered) {
+        for (int r = 0; r < gather.count; ++r) gather_vec4 = gather_vec4 && aligned(gather.bufs[r], 16);
+        gather_vec4 = gather_vec4 && ldc % 4 == 0;
     }
     int sm_count = 0, device = 0;
     cudaError_t err = current_device(&device, &sm_count);
@@ -224,7 +240,12 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     p.k = k;
     p.c = c;
     p.ldc = ldc;
-    p.c_vec4 = aligned(c, 16) && ldc % 4 == 0;
+    p.c_vec4 = gathered ? gather_vec4 : aligned(c, 16) && ldc % 4 == 0;
+    if (gathered) {
+        p.n_dst = gather.count;
+        for (int r = 0; r < gather.count; ++r) p.dst[r] = gather.bufs[r];
+        p.dst_row0 = static_cast<long long>(gather.rank) * m;
+    }
     const int tile_m = tk::gemm::kBlockM * cta_group;
     p.m_tiles = (m + tile_m - 1) / tile_m;
     p.n_tiles = (n + tk::gemm::kBlockN - 1) / tk::gemm::kBlockN;
@@ -239,7 +260,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     // problems): at least 4 K blocks per split, partials at most 64 MiB.
     p.k_splits = 1;
     p.kb_per_split = p.k_blocks;
-    if (!stats && tiles < sm_count / 2 && p.k_blocks >= 8) {
+    if (!stats && !gathered && tiles < sm_count / 2 && p.k_blocks >= 8) {
         int splits = static_cast<int>(sm_count / tiles);
         if (splits > p.k_blocks / 4) splits = p.k_blocks / 4;
         while (splits > 1 && static_cast<long long>(splits) * m * n * 4 > (64LL << 20)) --splits;
@@ -275,14 +296,17 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     using tk::gemm::kStatsMaxSum;
     using tk::gemm::kStatsNone;
     using tk::gemm::kStatsSoftmax;
+    using tk::gemm::kEpiGather;
     if (cta_group == 2) {
-        err = softmax ? launch_gemm_kernel<2, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
-              : stats ? launch_gemm_kernel<2, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
-                      : launch_gemm_kernel<2, kStatsNone>(ma, mb, p, device, sm_count, stream);
+        err = gathered ? launch_gemm_kernel<2, kEpiGather>(ma, mb, p, device, sm_count, stream)
+              : softmax ? launch_gemm_kernel<2, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
+              : stats   ? launch_gemm_kernel<2, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
+                        : launch_gemm_kernel<2, kStatsNone>(ma, mb, p, device, sm_count, stream);
     } else {
-        err = softmax ? launch_gemm_kernel<1, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
-              : stats ? launch_gemm_kernel<1, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
-                      : launch_gemm_kernel<1, kStatsNone>(ma, mb, p, device, sm_count, stream);
+        err = gathered ? launch_gemm_kernel<1, kEpiGather>(ma, mb, p, device, sm_count, stream)
+              : softmax ? launch_gemm_kernel<1, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
+              : stats   ? launch_gemm_kernel<1, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
+                        : launch_gemm_kernel<1, kStatsNone>(ma, mb, p, device, sm_count, stream);
     }
     if (softmax && err == cudaSuccess) {
         const bool vec4 = aligned(c, 16) && ldc % 4 == 0 && aligned(probs, 16) && ldp % 4 == 0;
@@ -438,6 +462,51 @@ cudaError_t tk_gemm_f16_f16_f32_nn_rowsoftmax(int m, int n, int k, const void* a
                                               int ldp, cudaStream_t stream) {
     if (probs == nullptr) return cudaErrorInvalidValue;
     return gemm_impl(m, n, k, a, lda, b, ldb, c, ldc, nullptr, nullptr, probs, ldp, stream);
+}
+
+cudaError_t tk_gemm_f16_f16_f32_nn_gather(int m, int n, int k, const void* a, int lda, const void* b,
+                                          int ldb, float* const* c_ranks, int n_ranks, int rank, int ldc,
+                                          cudaStream_t stream) {
+    if (c_ranks == nullptr || n_ranks < 1 || n_ranks > tk::gemm::kMaxGatherRanks || rank < 0 || rank >= n_ranks)
+        return cudaErrorInvalidValue;
+    for (int r = 0; r < n_ranks; ++r)
+        if (c_ranks[r] == nullptr) return cudaErrorInvalidValue;
+    if (m <= 0 || static_cast<long long>(n_ranks) * m > INT_MAX) return cudaErrorInvalidValue;
+    Gather g;
+    g.bufs = c_ranks;
+    g.count = n_ranks;
+    g.rank = rank;
+    float* local = c_ranks[rank] + static_cast<size_t>(rank) * m * static_cast<size_t>(ldc > 0 ? ldc : 0);
+    return gemm_impl(m, n, k, a, lda, b, ldb, local, ldc, nullptr, nullptr, nullptr, 0, stream, g);
+}
+
+cudaError_t tk_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+    if (ptr == nullptr || handle == nullptr || bytes == 0) return cudaErrorInvalidValue;
+    cudaError_t err = cudaMalloc(ptr, bytes);
+    if (err != cudaSuccess) return err;
+    err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+    if (err != cudaSuccess) {
+        static_cast<void>(cudaFree(*ptr));
+        *ptr = nullptr;
+    }
+    return err;
+}
+
+cudaError_t tk_ipc_open(const void* handle, void** ptr) {
+    if (ptr == nullptr || handle == nullptr) return cudaErrorInvalidValue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+cudaError_t tk_ipc_close(void* ptr) {
+    if (ptr == nullptr) return cudaErrorInvalidValue;
+    return cudaIpcCloseMemHandle(ptr);
+}
+
+cudaError_t tk_ipc_free(void* ptr) {
+    if (ptr == nullptr) return cudaErrorInvalidValue;
+    return cudaFree(ptr);
 }
 
 int tk_gemm_set_cta_group(int cta_group) {

@@ -34,6 +34,11 @@ SIGNATURES = {
     "tk_gemm_f16_f16_f32_nn_rowstats_noalloc": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _VP,
                                                      _VP]),
     "tk_gemm_f16_f16_f32_nn_rowsoftmax": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _VP, _I, _VP]),
+    "tk_gemm_f16_f16_f32_nn_gather": (_I, [_I, _I, _I, _VP, _I, _VP, _I, _VP, _I, _I, _I, _VP]),
+    "tk_ipc_alloc": (_I, [_SZ, C.POINTER(C.c_void_p), _VP]),
+    "tk_ipc_open": (_I, [_VP, C.POINTER(C.c_void_p)]),
+    "tk_ipc_close": (_I, [_VP]),
+    "tk_ipc_free": (_I, [_VP]),
     "tk_gemm_set_cta_group": (_I, [_I]),
     "tk_tile_row_sum_f32": (_I, [_VP, _SZ, _VP, _VP]),
     "tk_tile_row_max_f32": (_I, [_VP, _SZ, _VP, _VP]),
@@ -113,6 +118,36 @@ def gemm_rowstats_raw(m, n, k, a, lda, b, ldb, c, ldc, row_max, row_sum, stream=
 def gemm_rowsoftmax_raw(m, n, k, a, lda, b, ldb, c, ldc, probs, ldp, stream=None) -> int:
     return lib().tk_gemm_f16_f16_f32_nn_rowsoftmax(m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c), ldc,
                                                    _ptr(probs), ldp, _stream(stream))
+
+
+def gemm_gather_raw(m, n, k, a, lda, b, ldb, c_ranks, rank, ldc, stream=None) -> int:
+    """c_ranks: device pointers (ints) of every rank's gathered buffer, in rank order."""
+    arr = (C.c_void_p * len(c_ranks))(*c_ranks)
+    return lib().tk_gemm_f16_f16_f32_nn_gather(m, n, k, _ptr(a), lda, _ptr(b), ldb, C.cast(arr, C.c_void_p),
+                                                len(c_ranks), rank, ldc, _stream(stream))
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """Shareable device allocation: (pointer, 64-byte IPC handle)."""
+    ptr = C.c_void_p()
+    handle = C.create_string_buffer(64)
+    _check("tk_ipc_alloc", lib().tk_ipc_alloc(nbytes, C.byref(ptr), handle))
+    return ptr.value, handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = C.c_void_p()
+    buf = C.create_string_buffer(bytes(handle), 64)
+    _check("tk_ipc_open", lib().tk_ipc_open(buf, C.byref(ptr)))
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    _check("tk_ipc_close", lib().tk_ipc_close(ptr))
+
+
+def ipc_free(ptr: int) -> None:
+    _check("tk_ipc_free", lib().tk_ipc_free(ptr))
 
 
 def set_gemm_cta_group(g: int) -> int:

@@ -60,3 +60,53 @@ def gather_shards(local, total_rows: int, world: int, rank: int, rows_of, group=
     out = torch.cat(parts, dim=0)
     assert out.shape[0] == total_rows
     return out
+
+
+class _DeviceArray:
+    """A raw device buffer exposed through __cuda_array_interface__ (torch.as_tensor
+    wraps it without copying)."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3}
+
+
+class GatheredBuffer:
+    """Every rank's `rows x ld` FP32 gathered output, mapped into every rank's
+    process, for tk_gemm_f16_f16_f32_nn_gather (the all-gather fused into the GEMM
+    epilogue: each rank's kernel stores its row block straight into all ranks'
+    buffers over NVLink). Collective: every rank constructs it with the same shape.
+    `ptrs` lists the buffers in rank order (this rank's own allocation at `rank`);
+    `tensor()` is a torch view of this rank's buffer."""
+
+    def __init__(self, rows: int, ld: int, group=None):
+        import torch.distributed as dist
+
+        import tk_b200
+        self.rows, self.ld = rows, ld
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.own, handle = tk_b200.ipc_alloc(rows * ld * 4)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs = [self.own if r == self.rank else tk_b200.ipc_open(h) for r, h in enumerate(handles)]
+
+    def tensor(self):
+        import torch
+        return torch.as_tensor(_DeviceArray(self.own, (self.rows, self.ld)), device="cuda")
+
+    def close(self, group=None):
+        """Collective: unmaps the peers' buffers, waits until every rank has unmapped
+        this rank's, then frees it (an exported allocation must outlive its mappings).
+        Call once no rank's kernel writes into the buffers any more."""
+        import torch.distributed as dist
+
+        import tk_b200
+        if not self.ptrs:
+            return
+        for r, ptr in enumerate(self.ptrs):
+            if r != self.rank:
+                tk_b200.ipc_close(ptr)
+        dist.barrier(group=group)
+        tk_b200.ipc_free(self.own)
+        self.ptrs = []
