@@ -39,7 +39,15 @@
 namespace tk {
 namespace attn {
 
-constexpr int kThreads = 320;  // warps 0-7: two softmax warpgroups, 8: TMA, 9: MMA
+// Warps 0-7: two softmax warpgroups; warpgroup 2: warp 8 TMA, warp 9 MMA, warps 10-11
+// idle. Launched at 168 registers a thread (three warps share each SM sub-partition's
+// 16,384 registers), warpgroup 2 then gives registers up to the softmax warpgroups:
+// 128 x kRegsControl + 256 x kRegsSoftmax = 64,512 = 384 x 168, the launch's total.
+constexpr int kThreads = 384;
+constexpr int kRegsSoftmax = 208;
+constexpr int kRegsControl = (kThreads * 168 - 256 * kRegsSoftmax) / 128 / 8 * 8;
+static_assert(kRegsControl >= 24 && kRegsSoftmax % 8 == 0 && kRegsSoftmax <= 256, "setmaxnreg range");
+static_assert(128 * kRegsControl + 256 * kRegsSoftmax <= kThreads * 168, "register split above the launch total");
 constexpr int kBlockQ = 128;
 constexpr int kBlockKV = 128;
 constexpr int kKvSlots = 4;
@@ -47,7 +55,9 @@ constexpr uint32_t kTmemCols = 512;
 // In the unmasked fast path, one score pair in kPolyPairEvery takes exp2_poly2 on
 // the FMA pipe instead of two MUFU exponentials (0: none). Measured on B200 at
 // [8,32,4096,128]: every 4th / 3rd / 2nd pair gave 1061 / 1047 / 979 TFLOP/s
-// against 1124 with MUFU alone, so the default is none.
+// against 1124 with MUFU alone at 168 registers, and every 4th / 3rd pair
+// 1013-1034 / 990-1022 against 1109 with 208 registers (no spills), so the
+// default is none.
 #ifndef TK_ATTN_POLY_PAIR_EVERY
 #define TK_ATTN_POLY_PAIR_EVERY 0
 #endif
@@ -366,199 +376,206 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 8) {
-        // ---------------- TMA producer and scheduler (one thread) ----------------
-        if (lane == 0) {
-            tma_prefetch_desc(&map_q);
-            tma_prefetch_desc(&map_k);
-            tma_prefetch_desc(&map_v);
-            int slot = 0;
-            uint32_t phase = 0;
-            int issued = 0;
-            int items = 0;
-            bool ok = true;
-            int w = static_cast<int>(blockIdx.x);
-            for (int it_slot = 0;; it_slot ^= 1) {
-                if (items > 0) {
-                    w = p.next_item != nullptr ? static_cast<int>(gridDim.x) + atomicAdd(p.next_item, 1)
-                                               : w + static_cast<int>(gridDim.x);
-                }
-                const int wi = w < p.num_items ? w : -1;
-                // Entry it_slot was last used two items ago.
-                if (items >= 2 &&
-                    !mbar_wait(item_empty(it_slot), static_cast<uint32_t>((items - 2) >> 1) & 1u,
-                               kFaultProducerWait, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                item_info[it_slot] = wi;
-                mbar_arrive(item_full(it_slot));
-                if (wi < 0) break;
-                const Item it = make_item(wi, p);
-                // Q of the previous item is free once all its S MMAs have completed.
-                if (items > 0 &&
-                    !mbar_wait(q_empty, static_cast<uint32_t>(items - 1) & 1u, kFaultProducerWait, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                const int ntiles = it.has_tile1 ? 2 : 1;
-                mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
-                for (int g = 0; g < ntiles; ++g)
-                    for (int x = 0; x < C::kBoxes; ++x)
-                        tma_load_3d(base + C::kQOffset + g * C::kTileBytes + x * 16384, &map_q, q_full,
-                                    x * 64, it.q0 + g * kBlockQ, it.bh);
-                ++items;
-                for (int j = 0; j < it.n_blocks && ok; ++j) {
-                    for (int which = 0; which < 2; ++which) {  // K then V
-                        if (!mbar_wait(kv_empty(slot), phase ^ 1u, kFaultProducerWait, abort_flag)) {
-                            ok = false;
-                            break;
-                        }
-                        const uint32_t dst = base + C::kKvOffset + slot * C::kTileBytes;
-                        mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
+    // The register change sits inside each warpgroup's branch: ptxas sizes each
+    // branch's registers by the setmaxnreg that dominates it (one placed before the
+    // branches made it size all of them by the smallest).
+    if (warp >= 8) {
+        setmaxnreg_dec<kRegsControl>();
+        if (warp == 8) {
+            // ---------------- TMA producer and scheduler (one thread) ----------------
+            if (lane == 0) {
+                tma_prefetch_desc(&map_q);
+                tma_prefetch_desc(&map_k);
+                tma_prefetch_desc(&map_v);
+                int slot = 0;
+                uint32_t phase = 0;
+                int issued = 0;
+                int items = 0;
+                bool ok = true;
+                int w = static_cast<int>(blockIdx.x);
+                for (int it_slot = 0;; it_slot ^= 1) {
+                    if (items > 0) {
+                        w = p.next_item != nullptr ? static_cast<int>(gridDim.x) + atomicAdd(p.next_item, 1)
+                                                   : w + static_cast<int>(gridDim.x);
+                    }
+                    const int wi = w < p.num_items ? w : -1;
+                    // Entry it_slot was last used two items ago.
+                    if (items >= 2 &&
+                        !mbar_wait(item_empty(it_slot), static_cast<uint32_t>((items - 2) >> 1) & 1u,
+                                   kFaultProducerWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    item_info[it_slot] = wi;
+                    mbar_arrive(item_full(it_slot));
+                    if (wi < 0) break;
+                    const Item it = make_item(wi, p);
+                    // Q of the previous item is free once all its S MMAs have completed.
+                    if (items > 0 &&
+                        !mbar_wait(q_empty, static_cast<uint32_t>(items - 1) & 1u, kFaultProducerWait, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const int ntiles = it.has_tile1 ? 2 : 1;
+                    mbar_arrive_expect_tx(q_full, ntiles * C::kTileBytes);
+                    for (int g = 0; g < ntiles; ++g)
                         for (int x = 0; x < C::kBoxes; ++x)
-                            tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
-                                        x * 64, j * kBlockKV, it.bh_kv);
-                        ++issued;
-                        if (++slot == kKvSlots) {
-                            slot = 0;
-                            phase ^= 1u;
+                            tma_load_3d(base + C::kQOffset + g * C::kTileBytes + x * 16384, &map_q, q_full,
+                                        x * 64, it.q0 + g * kBlockQ, it.bh);
+                    ++items;
+                    for (int j = 0; j < it.n_blocks && ok; ++j) {
+                        for (int which = 0; which < 2; ++which) {  // K then V
+                            if (!mbar_wait(kv_empty(slot), phase ^ 1u, kFaultProducerWait, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            const uint32_t dst = base + C::kKvOffset + slot * C::kTileBytes;
+                            mbar_arrive_expect_tx(kv_full(slot), C::kTileBytes);
+                            for (int x = 0; x < C::kBoxes; ++x)
+                                tma_load_3d(dst + x * 16384, which == 0 ? &map_k : &map_v, kv_full(slot),
+                                            x * 64, j * kBlockKV, it.bh_kv);
+                            ++issued;
+                            if (++slot == kKvSlots) {
+                                slot = 0;
+                                phase ^= 1u;
+                            }
                         }
                     }
+                    if (!ok) break;
                 }
-                if (!ok) break;
-            }
-            if (!ok) {
-                // Let every issued load land before the CTA may exit: the last Q load
-                // and the last (up to kKvSlots) K/V loads.
-                if (items > 0) mbar_wait(q_full, static_cast<uint32_t>(items - 1) & 1u, kFaultDrainWait, nullptr);
-                int s = slot;
-                uint32_t ph = phase;
-                for (int i = 0; i < min(issued, kKvSlots); ++i) {
-                    if (--s < 0) {
-                        s = kKvSlots - 1;
-                        ph ^= 1u;
+                if (!ok) {
+                    // Let every issued load land before the CTA may exit: the last Q load
+                    // and the last (up to kKvSlots) K/V loads.
+                    if (items > 0) mbar_wait(q_full, static_cast<uint32_t>(items - 1) & 1u, kFaultDrainWait, nullptr);
+                    int s = slot;
+                    uint32_t ph = phase;
+                    for (int i = 0; i < min(issued, kKvSlots); ++i) {
+                        if (--s < 0) {
+                            s = kKvSlots - 1;
+                            ph ^= 1u;
+                        }
+                        mbar_wait(kv_full(s), ph, kFaultDrainWait, nullptr);
                     }
-                    mbar_wait(kv_full(s), ph, kFaultDrainWait, nullptr);
                 }
             }
-        }
-        __syncwarp();
-    } else if (warp == 9) {
-        // ---------------- MMA issuer (one thread) ----------------
-        // Issue order per key block j: S0_j, PV1_{j-1}, S1_j, PV0_j. Before PV0_j the
-        // thread also waits for K_{j+1}, so PV0_j and S0_{j+1} go to the tensor pipe
-        // back to back: the chain PV0_j -> S0_{j+1} -> softmax 0 is the critical path.
-        if (lane == 0) {
-            const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
-            auto kv_addr = [&](int slot) { return base + C::kKvOffset + slot * C::kTileBytes; };
-            auto issue_s = [&](int g, uint32_t k_addr) {
-#pragma unroll
-                for (int kk = 0; kk < kDPad / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    mma_f16_ss<1>(tmem + 256u * g, sw128_desc(q_addr[g] + off, 16, 1024),
-                                  sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
-                }
-                mma_commit(s_full(g));
-            };
-            auto issue_pv = [&](int g, uint32_t v_addr, bool first) {
-#pragma unroll
-                for (int kk = 0; kk < kBlockKV / 16; ++kk)
-                    mma_f16_ts(tmem + 256u * g + 128u, tmem + 256u * g + kk * 8,
-                               sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
-                               (!first || kk > 0) ? 1u : 0u);
-            };
-            uint32_t pr_phase[2] = {0, 0};
-            int done[2] = {0, 0};  // items in which tile g has produced an output
-            int kv_base = 0;       // K/V loads of the previous items
-            int items = 0;
-            bool ok = true;
-            // The first PV of tile g in an item overwrites O_g: the softmax warps must
-            // have read the previous item's O_g out of tensor memory.
-            auto o_free = [&](int g) {
-                return done[g] == 0 ||
-                       mbar_wait(o_empty(g), static_cast<uint32_t>(done[g] - 1) & 1u, kFaultAttnWait, abort_flag);
-            };
-            for (int it_slot = 0; ok; it_slot ^= 1, ++items) {
-                if (!mbar_wait(item_full(it_slot), static_cast<uint32_t>(items >> 1) & 1u, kFaultAttnWait,
-                               abort_flag))
-                    break;
-                const int wi = item_info[it_slot];
-                mbar_arrive(item_empty(it_slot));
-                if (wi < 0) break;
-                const Item it = make_item(wi, p);
-                auto kv_slot = [&](int load) { return (kv_base + load) % kKvSlots; };
-                auto kv_phase = [&](int load) { return static_cast<uint32_t>((kv_base + load) / kKvSlots) & 1u; };
-                ok = mbar_wait(q_full, static_cast<uint32_t>(items) & 1u, kFaultAttnWait, abort_flag) &&
-                     mbar_wait(kv_full(kv_slot(0)), kv_phase(0), kFaultAttnWait, abort_flag);
-                tc_fence_after();
-                if (ok) issue_s(0, kv_addr(kv_slot(0)));
-                const int n_blocks = it.n_blocks;
-                for (int j = 0; j < n_blocks && ok; ++j) {
-                    ok = false;
-                    const int k_slot = kv_slot(2 * j);
-                    const int v_slot = kv_slot(2 * j + 1);
-                    const int prev_v_slot = kv_slot(2 * j - 1 + kKvSlots) ;
-                    const bool last = j == n_blocks - 1;
-                    const bool tile0 = j < it.n_blocks0;
-                    // PV1_{j-1}, then V_{j-1} is free
-                    if (j > 0) {
-                        if (it.has_tile1) {
-                            if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                            pr_phase[1] ^= 1u;
-                            if (j == 1 && !o_free(1)) break;
+            __syncwarp();
+        } else if (warp == 9) {
+            // ---------------- MMA issuer (one thread) ----------------
+            // Issue order per key block j: S0_j, PV1_{j-1}, S1_j, PV0_j. Before PV0_j the
+            // thread also waits for K_{j+1}, so PV0_j and S0_{j+1} go to the tensor pipe
+            // back to back: the chain PV0_j -> S0_{j+1} -> softmax 0 is the critical path.
+            if (lane == 0) {
+                const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
+                auto kv_addr = [&](int slot) { return base + C::kKvOffset + slot * C::kTileBytes; };
+                auto issue_s = [&](int g, uint32_t k_addr) {
+    #pragma unroll
+                    for (int kk = 0; kk < kDPad / 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                        mma_f16_ss<1>(tmem + 256u * g, sw128_desc(q_addr[g] + off, 16, 1024),
+                                      sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
+                    }
+                    mma_commit(s_full(g));
+                };
+                auto issue_pv = [&](int g, uint32_t v_addr, bool first) {
+    #pragma unroll
+                    for (int kk = 0; kk < kBlockKV / 16; ++kk)
+                        mma_f16_ts(tmem + 256u * g + 128u, tmem + 256u * g + kk * 8,
+                                   sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
+                                   (!first || kk > 0) ? 1u : 0u);
+                };
+                uint32_t pr_phase[2] = {0, 0};
+                int done[2] = {0, 0};  // items in which tile g has produced an output
+                int kv_base = 0;       // K/V loads of the previous items
+                int items = 0;
+                bool ok = true;
+                // The first PV of tile g in an item overwrites O_g: the softmax warps must
+                // have read the previous item's O_g out of tensor memory.
+                auto o_free = [&](int g) {
+                    return done[g] == 0 ||
+                           mbar_wait(o_empty(g), static_cast<uint32_t>(done[g] - 1) & 1u, kFaultAttnWait, abort_flag);
+                };
+                for (int it_slot = 0; ok; it_slot ^= 1, ++items) {
+                    if (!mbar_wait(item_full(it_slot), static_cast<uint32_t>(items >> 1) & 1u, kFaultAttnWait,
+                                   abort_flag))
+                        break;
+                    const int wi = item_info[it_slot];
+                    mbar_arrive(item_empty(it_slot));
+                    if (wi < 0) break;
+                    const Item it = make_item(wi, p);
+                    auto kv_slot = [&](int load) { return (kv_base + load) % kKvSlots; };
+                    auto kv_phase = [&](int load) { return static_cast<uint32_t>((kv_base + load) / kKvSlots) & 1u; };
+                    ok = mbar_wait(q_full, static_cast<uint32_t>(items) & 1u, kFaultAttnWait, abort_flag) &&
+                         mbar_wait(kv_full(kv_slot(0)), kv_phase(0), kFaultAttnWait, abort_flag);
+                    tc_fence_after();
+                    if (ok) issue_s(0, kv_addr(kv_slot(0)));
+                    const int n_blocks = it.n_blocks;
+                    for (int j = 0; j < n_blocks && ok; ++j) {
+                        ok = false;
+                        const int k_slot = kv_slot(2 * j);
+                        const int v_slot = kv_slot(2 * j + 1);
+                        const int prev_v_slot = kv_slot(2 * j - 1 + kKvSlots) ;
+                        const bool last = j == n_blocks - 1;
+                        const bool tile0 = j < it.n_blocks0;
+                        // PV1_{j-1}, then V_{j-1} is free
+                        if (j > 0) {
+                            if (it.has_tile1) {
+                                if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                                pr_phase[1] ^= 1u;
+                                if (j == 1 && !o_free(1)) break;
+                                tc_fence_after();
+                                issue_pv(1, kv_addr(prev_v_slot), j == 1);
+                            }
+                            mma_commit(kv_empty(prev_v_slot));
+                        }
+                        // S1_j, then K_j is free. K_j was waited for before S0_j, unless
+                        // tile 0 has already finished.
+                        if (!tile0 && !mbar_wait(kv_full(k_slot), kv_phase(2 * j), kFaultAttnWait, abort_flag)) break;
+                        if (it.has_tile1) issue_s(1, kv_addr(k_slot));
+                        mma_commit(kv_empty(k_slot));
+                        // After the item's last S MMA, Q may be replaced by the next item's.
+                        if (last) mma_commit(q_empty);
+                        // PV0_j and S0_{j+1}, back to back
+                        if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
+                        if (tile0) {
+                            const bool tile0_last = j == it.n_blocks0 - 1;
+                            const int next_k_slot = kv_slot(2 * j + 2);
+                            if (!tile0_last &&
+                                !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
+                                break;
+                            if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
+                            pr_phase[0] ^= 1u;
+                            if (j == 0 && !o_free(0)) break;
                             tc_fence_after();
-                            issue_pv(1, kv_addr(prev_v_slot), j == 1);
+                            issue_pv(0, kv_addr(v_slot), j == 0);
+                            if (tile0_last) {
+                                mma_commit(o_final(0));
+                            } else {
+                                issue_s(0, kv_addr(next_k_slot));
+                            }
                         }
-                        mma_commit(kv_empty(prev_v_slot));
-                    }
-                    // S1_j, then K_j is free. K_j was waited for before S0_j, unless
-                    // tile 0 has already finished.
-                    if (!tile0 && !mbar_wait(kv_full(k_slot), kv_phase(2 * j), kFaultAttnWait, abort_flag)) break;
-                    if (it.has_tile1) issue_s(1, kv_addr(k_slot));
-                    mma_commit(kv_empty(k_slot));
-                    // After the item's last S MMA, Q may be replaced by the next item's.
-                    if (last) mma_commit(q_empty);
-                    // PV0_j and S0_{j+1}, back to back
-                    if (!mbar_wait(kv_full(v_slot), kv_phase(2 * j + 1), kFaultAttnWait, abort_flag)) break;
-                    if (tile0) {
-                        const bool tile0_last = j == it.n_blocks0 - 1;
-                        const int next_k_slot = kv_slot(2 * j + 2);
-                        if (!tile0_last &&
-                            !mbar_wait(kv_full(next_k_slot), kv_phase(2 * j + 2), kFaultAttnWait, abort_flag))
-                            break;
-                        if (!mbar_wait(p_ready(0), pr_phase[0], kFaultAttnWait, abort_flag)) break;
-                        pr_phase[0] ^= 1u;
-                        if (j == 0 && !o_free(0)) break;
-                        tc_fence_after();
-                        issue_pv(0, kv_addr(v_slot), j == 0);
-                        if (tile0_last) {
-                            mma_commit(o_final(0));
-                        } else {
-                            issue_s(0, kv_addr(next_k_slot));
+                        if (last) {
+                            // PV1_last
+                            if (it.has_tile1) {
+                                if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
+                                pr_phase[1] ^= 1u;
+                                if (j == 0 && !o_free(1)) break;
+                                tc_fence_after();
+                                issue_pv(1, kv_addr(v_slot), j == 0);
+                                mma_commit(o_final(1));
+                            }
+                            mma_commit(kv_empty(v_slot));
                         }
+                        ok = true;
                     }
-                    if (last) {
-                        // PV1_last
-                        if (it.has_tile1) {
-                            if (!mbar_wait(p_ready(1), pr_phase[1], kFaultAttnWait, abort_flag)) break;
-                            pr_phase[1] ^= 1u;
-                            if (j == 0 && !o_free(1)) break;
-                            tc_fence_after();
-                            issue_pv(1, kv_addr(v_slot), j == 0);
-                            mma_commit(o_final(1));
-                        }
-                        mma_commit(kv_empty(v_slot));
-                    }
-                    ok = true;
+                    ++done[0];
+                    if (it.has_tile1) ++done[1];
+                    kv_base += 2 * n_blocks;
                 }
-                ++done[0];
-                if (it.has_tile1) ++done[1];
-                kv_base += 2 * n_blocks;
             }
+            __syncwarp();
         }
-        __syncwarp();
-    } else if (warp < 8) {
+    } else {
+        setmaxnreg_inc<kRegsSoftmax>();
         // ---------------- softmax warpgroups (warps 0-3: tile 0, 4-7: tile 1) ----------------
         const int g = static_cast<int>(warp >> 2);
         const uint32_t quarter = warp & 3u;

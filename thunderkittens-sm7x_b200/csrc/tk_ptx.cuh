@@ -350,6 +350,18 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, int a_mn, int
            | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// Per-warpgroup register reallocation: every warp of a warpgroup executes the same
+// one. An increase waits until decreases elsewhere in the CTA have freed enough of
+// the registers the CTA was launched with.
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 __device__ __forceinline__ uint32_t warp_id() {
     return __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0);
