@@ -148,6 +148,15 @@ TK_API cudaError_t tk_ipc_free(void* ptr);
  * the previous setting. */
 TK_API int tk_gemm_set_cta_group(int cta_group);
 
+/* Tuning knob, no counterpart in the reference: how split-K GEMMs (few output
+ * tiles, long K) sum their K splits. 0 = inside the kernel, the splits of one
+ * tile forming a thread-block cluster, whenever all tiles' clusters fit on the
+ * GPU at once (default); 1 = always a second kernel over partials in scratch.
+ * The split count does not depend on the mode and both add the splits in the
+ * same order, so results are bit-identical. Process-wide; returns the previous
+ * setting. */
+TK_API int tk_gemm_set_splitk_reduce(int mode);
+
 /* ---- tile row operations --------------------------------------------------- */
 /* `tiles` holds n_tiles contiguous 16x16 row-major FP32 tiles (256 floats,
  * 1 KiB each). Reductions write 16 floats per tile (row order); softmax writes

@@ -168,10 +168,10 @@ def test_decode_16x4096x4096():
                                                  (304, 512, 4096, 520, 2), (16, 4096, 4096, 4096, 0)],
                          ids=["ragged_n_scalar_c", "pairs_off", "cta_pairs", "decode"])
 def test_split_k_in_kernel_reduction(m, n, k, ldc, cta_group):
-    """Split-K shapes (few output tiles, long K): the CTA that completes a tile's
-    last split sums the partials in split order. Results within the error bound,
-    C padding untouched, and bit-identical across two runs (the order does not
-    depend on which CTA finishes last)."""
+    """Split-K shapes (few output tiles, long K): the partials of a tile's K splits
+    are summed in split order, inside the tile's cluster (up to 8 splits on single
+    CTAs) or by a second kernel. Results within the error bound, C padding untouched,
+    and bit-identical across two runs (the order does not depend on timing)."""
     a, b = oracle.gen_gemm_normal(5, 0.02, m, n, k, k, n)
     sentinel = np.float32(-7.0)
     c1 = run_gemm(m, n, k, a, k, b, n, ldc, sentinel=sentinel, cta_group=cta_group)
@@ -180,6 +180,29 @@ def test_split_k_in_kernel_reduction(m, n, k, ldc, cta_group):
     assert np.all(c1[:, n:] == sentinel)
     r, s = oracle.gemm_ref(m, n, k, a, k, b, n)
     assert oracle.gemm_check(k, np.ascontiguousarray(c1[:, :n]), r, s, n, n)[0] == 0
+    assert tk_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("m,n,k,ldc", [(16, 4096, 4096, 4096), (48, 784, 2048, 787), (512, 512, 512, 512),
+                                       (1024, 1024, 1024, 1032), (208, 1040, 1024, 1040)],
+                         ids=["decode_8_splits", "ragged_scalar_c", "512_2_splits", "1024_4_splits_ldc",
+                              "ragged_rows_cols"])
+def test_split_k_cluster_reduction_matches_kernel(m, n, k, ldc):
+    """The in-cluster split-K reduction (the K splits of a tile form a cluster and sum
+    their partials over distributed shared memory) and the separate reduction kernel
+    add the same partials in the same order: bit-identical C, padding untouched."""
+    a, b = oracle.gen_gemm_normal(7, 0.02, m, n, k, k, n)
+    sentinel = np.float32(-5.0)
+    prev = tk_b200.set_gemm_splitk_reduce(1)
+    try:
+        c_kernel = run_gemm(m, n, k, a, k, b, n, ldc, sentinel=sentinel)
+        tk_b200.set_gemm_splitk_reduce(0)
+        c_cluster = run_gemm(m, n, k, a, k, b, n, ldc, sentinel=sentinel)
+    finally:
+        tk_b200.set_gemm_splitk_reduce(prev)
+    assert np.array_equal(c_cluster.view(np.uint32), c_kernel.view(np.uint32))
+    assert np.all(c_cluster[:, n:] == sentinel)
+    check_rows(m, n, k, a, k, b, n, c_cluster, ldc, sample_rows(m, 16))
     assert tk_b200.device_status() == 0
 
 

@@ -122,7 +122,17 @@ enum Stats : int {
     kStatsMaxSum = 1,   // (row max, row sum) of the tile's columns, fixed pairwise order
     kStatsSoftmax = 2,  // (row max m_t, sum of exp(c - m_t)) for a full-row softmax
     kEpiGather = 3,     // no statistics; each row stored to every Params::dst (multi-GPU all-gather)
+    // Split-K reduced inside the cluster: the k_splits CTAs of one output tile form a
+    // cluster (CTA rank = split index, one work unit per CTA). Each leaves its partial
+    // tile in its own shared memory; after a cluster barrier every CTA sums its share
+    // of the tile over all splits in split order (distributed shared memory) into C.
+    kEpiSplitCluster = 4,
 };
+
+// Row pitch (floats) of a partial tile in shared memory for kEpiSplitCluster: 16
+// bytes over a whole number of bank rows, so the 32 lanes' 16-byte stores of one
+// column quad fall on distinct banks eight lanes at a time.
+constexpr int kRedStride = kBlockN + 4;
 
 template <int kCtaGroup, int kStats>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -307,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 static_cast<long long>(tm) * C::kTileM + rank * kBlockM + warp * 32 + lane;
             const int col_base = tn * kBlockN;
             const bool row_ok = row < p.m;
-            const bool split = p.k_splits > 1;
+            const bool split = kStats != kEpiSplitCluster && p.k_splits > 1;
             float* crow = split ? p.ws + (static_cast<long long>(t % p.k_splits) * p.m + row) * p.n
                                 : p.c + row * p.ldc;
             const bool vec4 = split || p.c_vec4;
@@ -344,7 +354,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     __syncwarp();
                 }
-                constexpr int kDsts = kStats == kEpiGather ? 0 : 1;
+                if constexpr (kStats == kEpiSplitCluster) {
+                    // Partial rows stay in this CTA's shared memory (the pipeline stages
+                    // are idle: every load of the CTA's one work unit has been consumed).
+                    if (row_ok) {
+                        float* prow = reinterpret_cast<float*>(smem) + (warp * 32 + lane) * kRedStride + chunk * 32;
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            *reinterpret_cast<float4*>(prow + 4 * q) =
+                                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                    }
+                }
+                constexpr int kDsts = (kStats == kEpiGather || kStats == kEpiSplitCluster) ? 0 : 1;
 #pragma unroll
                 for (int d = 0; d < kDsts; ++d) {
                     float* const drow = crow;
@@ -432,6 +454,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_before();
     __syncthreads();
     if constexpr (kCtaGroup == 2) cluster_sync();
+    if constexpr (kStats == kEpiSplitCluster) {
+        static_assert(kCtaGroup == 1, "the in-cluster split-K reduction runs on single-CTA tiles");
+        static_assert(kBlockM * kRedStride * 4 <= Cfg<kCtaGroup>::kStages * Cfg<kCtaGroup>::kStageBytes,
+                      "partial tile larger than the pipeline stages");
+        // Every CTA reaches both barriers, also after a timed-out wait (its partial is
+        // then not used: the fault is recorded and the call reports it).
+        cluster_sync();  // every split's partial is in its CTA's shared memory
+        int tm, tn, kb0, kb1;
+        work_coords(static_cast<int>(blockIdx.x), p, &tm, &tn, &kb0, &kb1);
+        const int rows = min(kBlockM, p.m - tm * kBlockM);
+        const int quads_per_row = min(kBlockN, p.n - tn * kBlockN) / 4;
+        const int quads = rows * quads_per_row;
+        const int my = static_cast<int>(cluster_ctarank());
+        const int q_end = quads * (my + 1) / p.k_splits;
+        for (int q = quads * my / p.k_splits + static_cast<int>(threadIdx.x); q < q_end; q += kThreads) {
+            const int r = q / quads_per_row;
+            const int c4 = (q - r * quads_per_row) * 4;
+            const uint32_t local = base + static_cast<uint32_t>((r * kRedStride + c4) * 4);
+            // Split order, as splitk_reduce_kernel: bit-identical results.
+            float4 acc = ld_shared_cluster_f4(mapa_shared(local, 0));
+            for (int sp = 1; sp < p.k_splits; ++sp) {
+                const float4 v = ld_shared_cluster_f4(mapa_shared(local, static_cast<uint32_t>(sp)));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            float* dst = p.c + (static_cast<long long>(tm) * kBlockM + r) * p.ldc + tn * kBlockN + c4;
+            if (p.c_vec4) {
+                *reinterpret_cast<float4*>(dst) = acc;
+            } else {
+                dst[0] = acc.x;
+                dst[1] = acc.y;
+                dst[2] = acc.z;
+                dst[3] = acc.w;
+            }
+        }
+        cluster_sync();  // no CTA leaves while another still reads its shared memory
+    }
     if (warp == 5) {
         tc_fence_after();
         tmem_dealloc<kCtaGroup>(tmem_base, kTmemCols);

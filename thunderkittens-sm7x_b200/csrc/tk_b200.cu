@@ -145,6 +145,66 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
 }
 
+int g_gemm_splitk_mode = 0;  // 0 = in-cluster reduction where it fits, 1 = always the separate kernel
+
+// Split-K with the reduction inside the kernel: grid = every work unit, clusters
+// of k_splits CTAs (one output tile each).
+cudaError_t launch_gemm_split_cluster(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
+                                      int device, cudaStream_t stream) {
+    using Cfg = tk::gemm::Cfg<1>;
+    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster>;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(p.num_tiles));
+    cfg.blockDim = dim3(tk::gemm::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(p.k_splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
+}
+
+// How many clusters of `splits` CTAs of the in-cluster split-K kernel can be
+// resident at once on `device` (cached; 0 when the query fails).
+int split_cluster_capacity(int device, int splits) {
+    static std::atomic<int> cache[tk::host::kMaxDevices][9];
+    static std::atomic<bool> configured[tk::host::kMaxDevices];
+    int v = cache[device][splits].load(std::memory_order_acquire);
+    if (v != 0) return v < 0 ? 0 : v;
+    using Cfg = tk::gemm::Cfg<1>;
+    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster>;
+    if (!configured[device].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+            cudaSuccess) {
+            static_cast<void>(cudaGetLastError());
+            return 0;
+        }
+        configured[device].store(true, std::memory_order_release);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(splits));
+    cfg.blockDim = dim3(tk::gemm::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+        static_cast<void>(cudaGetLastError());
+        clusters = 0;
+    }
+    cache[device][splits].store(clusters > 0 ? clusters : -1, std::memory_order_release);
+    return clusters;
+}
+
 // Destinations of the multi-GPU gathered GEMM: rank `rank` of `count` writes its m
 // rows at row rank * m of each buffer (count == 0: an ordinary GEMM into c).
 struct Gather {
@@ -269,9 +329,27 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
             p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
         }
     }
+    // On single-CTA tiles the split count is lowered, if needed, to the largest one
+    // (at most 8: the portable cluster size) whose tile clusters can all be resident
+    // at once; the splits of a tile then reduce inside their cluster. Otherwise the
+    // partials go through scratch to splitk_reduce_kernel. Both add the same splits
+    // in the same order, so the reduction mode does not change the results.
+    bool cluster_fits = false;
+    if (p.k_splits > 1 && cta_group == 1) {
+        for (int s = p.k_splits < 8 ? p.k_splits : 8; s >= 2 && !cluster_fits; --s) {
+            const int kb_per = (p.k_blocks + s - 1) / s;
+            const int splits = (p.k_blocks + kb_per - 1) / kb_per;
+            if (splits >= 2 && tiles <= split_cluster_capacity(device, splits)) {
+                p.kb_per_split = kb_per;
+                p.k_splits = splits;
+                cluster_fits = true;
+            }
+        }
+    }
+    const bool cluster_reduce = cluster_fits && g_gemm_splitk_mode == 0;
     p.num_tiles = static_cast<int>(tiles) * p.k_splits;
     p.ws = nullptr;
-    if (p.k_splits > 1) {
+    if (p.k_splits > 1 && !cluster_reduce) {
         err = tk::host::scratch_alloc(reinterpret_cast<void**>(&p.ws),
                                       static_cast<size_t>(p.k_splits) * m * n * sizeof(float), device, stream);
         if (err != cudaSuccess) {
@@ -297,7 +375,9 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     using tk::gemm::kStatsNone;
     using tk::gemm::kStatsSoftmax;
     using tk::gemm::kEpiGather;
-    if (cta_group == 2) {
+    if (cluster_reduce) {
+        err = launch_gemm_split_cluster(ma, mb, p, device, stream);
+    } else if (cta_group == 2) {
         err = gathered ? launch_gemm_kernel<2, kEpiGather>(ma, mb, p, device, sm_count, stream)
               : softmax ? launch_gemm_kernel<2, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
               : stats   ? launch_gemm_kernel<2, kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
@@ -318,7 +398,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         tk::gemm::rowstats_finish_kernel<<<(m + 255) / 256, 256, 0, stream>>>(
             reinterpret_cast<const float2*>(partial), m, p.n_tiles, row_max, row_sum);
     }
-    if (p.k_splits > 1) {
+    if (p.k_splits > 1 && !cluster_reduce) {
         if (err == cudaSuccess) {
             const long long quads = static_cast<long long>(m) * (n / 4);
             const int blocks = static_cast<int>(quads / 256 + 1 < 4 * sm_count ? quads / 256 + 1 : 4 * sm_count);
@@ -512,6 +592,12 @@ cudaError_t tk_ipc_free(void* ptr) {
 int tk_gemm_set_cta_group(int cta_group) {
     const int prev = g_gemm_cta_group_override;
     if (cta_group >= 0 && cta_group <= 2) g_gemm_cta_group_override = cta_group;
+    return prev;
+}
+
+int tk_gemm_set_splitk_reduce(int mode) {
+    const int prev = g_gemm_splitk_mode;
+    if (mode == 0 || mode == 1) g_gemm_splitk_mode = mode;
     return prev;
 }
 

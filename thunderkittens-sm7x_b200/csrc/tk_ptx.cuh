@@ -137,6 +137,16 @@ __device__ __forceinline__ void cluster_sync() {
                  ::: "memory");
 }
 
+// 16-byte load from the shared memory of a CTA of the cluster (address from mapa).
+__device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
+}
+
 // ---- TMA ----------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_desc(const void* map) {

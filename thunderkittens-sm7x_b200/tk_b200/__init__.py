@@ -40,6 +40,7 @@ SIGNATURES = {
     "tk_ipc_close": (_I, [_VP]),
     "tk_ipc_free": (_I, [_VP]),
     "tk_gemm_set_cta_group": (_I, [_I]),
+    "tk_gemm_set_splitk_reduce": (_I, [_I]),
     "tk_tile_row_sum_f32": (_I, [_VP, _SZ, _VP, _VP]),
     "tk_tile_row_max_f32": (_I, [_VP, _SZ, _VP, _VP]),
     "tk_tile_row_softmax_f32": (_I, [_VP, _SZ, _VP, _VP]),
@@ -152,6 +153,12 @@ def ipc_free(ptr: int) -> None:
 
 def set_gemm_cta_group(g: int) -> int:
     return lib().tk_gemm_set_cta_group(g)
+
+
+def set_gemm_splitk_reduce(mode: int) -> int:
+    """0: split-K partials summed inside the kernel (tile clusters) where they fit;
+    1: always by a second kernel. Returns the previous mode."""
+    return lib().tk_gemm_set_splitk_reduce(mode)
 
 
 def attention_16x16_raw(q, k, v, out, causal=False, stream=None) -> int:
