@@ -185,12 +185,13 @@ def test_split_k_in_kernel_reduction(m, n, k, ldc, cta_group):
 
 @pytest.mark.parametrize("m,n,k,ldc", [(16, 4096, 4096, 4096), (48, 784, 2048, 787), (512, 512, 512, 512),
                                        (1024, 1024, 1024, 1032), (208, 1040, 1024, 1040)],
-                         ids=["decode_8_splits", "ragged_scalar_c", "512_2_splits", "1024_4_splits_ldc",
-                              "ragged_rows_cols"])
+                         ids=["decode", "ragged_scalar_c_128_cols", "512_128_cols", "1024_4_splits_ldc",
+                              "ragged_rows_cols_128_cols"])
 def test_split_k_cluster_reduction_matches_kernel(m, n, k, ldc):
     """The in-cluster split-K reduction (the K splits of a tile form a cluster and sum
     their partials over distributed shared memory) and the separate reduction kernel
-    add the same partials in the same order: bit-identical C, padding untouched."""
+    add the same partials in the same order: bit-identical C, padding untouched. The
+    shapes cover 256- and 128-column tiles and A boxes of fewer than 128 rows."""
     a, b = oracle.gen_gemm_normal(7, 0.02, m, n, k, k, n)
     sentinel = np.float32(-5.0)
     prev = tk_b200.set_gemm_splitk_reduce(1)

@@ -31,28 +31,32 @@ namespace tk {
 namespace gemm {
 
 constexpr int kBlockM = 128;   // rows of C per CTA
-constexpr int kBlockN = 256;   // MMA N: columns of C per tile
+constexpr int kBlockN = 256;   // MMA N: columns of C per tile (128 in the small-M split-K variant)
 constexpr int kBlockK = 64;    // K per pipeline stage (one 128-byte swizzle row)
 constexpr int kMmaK = 16;      // K per tcgen05.mma (kind::f16)
 constexpr int kGroupM = 16;    // tile-rows per rasterisation group
 constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
-constexpr uint32_t kTmemCols = 512;  // two 256-column FP32 accumulators
 constexpr int kMaxGatherRanks = 8;   // destinations of the all-gather epilogue
 
-template <int kCtaGroup>
+template <int kCtaGroup, int kBN = kBlockN>
 struct Cfg {
     static constexpr int kTileM = kBlockM * kCtaGroup;        // rows per tile (per cluster)
-    static constexpr int kBCols = kBlockN / kCtaGroup;        // B columns loaded per CTA
+    static constexpr int kBCols = kBN / kCtaGroup;            // B columns loaded per CTA
     static constexpr int kABytes = kBlockM * kBlockK * 2;     // 16 KiB
     static constexpr int kBBytes = kBlockK * kBCols * 2;      // 32 or 16 KiB
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = kCtaGroup == 1 ? 4 : 6;
+    static constexpr int kStages = (kCtaGroup == 1 && kBN == 256) ? 4 : 6;
+    static constexpr uint32_t kTmemCols = 2 * kBN;            // two FP32 accumulators
+    // Row pitch (floats) of a partial tile in shared memory for kEpiSplitCluster: 16
+    // bytes over a whole number of bank rows, so the 32 lanes' 16-byte stores of one
+    // column quad fall on distinct banks eight lanes at a time.
+    static constexpr int kRedStride = kBN + 4;
     static constexpr int kBarrierBytes = 256;
     // kEpiGather: a 32 x 33-float transpose buffer per epilogue warp, so that the
     // stores into the ranks' buffers are whole 128-byte row segments.
     static constexpr int kXposeBytes = 4 * 32 * 33 * 4;
     static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + kXposeBytes + 1024;  // + align slack
-    static constexpr uint32_t kIdesc = idesc_f16_f32(kBlockM * kCtaGroup, kBlockN, 0, 1);
+    static constexpr uint32_t kIdesc = idesc_f16_f32(kBlockM * kCtaGroup, kBN, 0, 1);
 };
 
 struct Params {
@@ -67,6 +71,10 @@ struct Params {
     // sums the splits in order into C (deterministic). k_splits == 1 writes C directly.
     int k_splits, kb_per_split;
     float* ws;
+    // Rows of A per TMA box (single-CTA tiles; 0 = kBlockM). When all of M fits one
+    // tile, only round_up(M, 16) rows are fetched: the MMA's other rows read stale
+    // shared memory and only produce accumulator rows that are never stored.
+    int a_box_rows;
     // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
     float* partial;     // [m][n_tiles][2] (max, sum), or null
     // kEpiGather: row r of this GEMM goes to row dst_row0 + r of every dst[0..n_dst)
@@ -129,16 +137,14 @@ enum Stats : int {
     kEpiSplitCluster = 4,
 };
 
-// Row pitch (floats) of a partial tile in shared memory for kEpiSplitCluster: 16
-// bytes over a whole number of bank rows, so the 32 lanes' 16-byte stores of one
-// column quad fall on distinct banks eight lanes at a time.
-constexpr int kRedStride = kBlockN + 4;
 
-template <int kCtaGroup, int kStats>
+template <int kCtaGroup, int kStats, int kBN = kBlockN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const Params p) {
-    using C = Cfg<kCtaGroup>;
+    using C = Cfg<kCtaGroup, kBN>;
+    static_assert(kBN == kBlockN || ((kStats == kStatsNone || kStats == kEpiSplitCluster) && kCtaGroup == 1),
+                  "128-column tiles only for plain single-CTA tiles");
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -176,7 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&map_b);
     }
     if (warp == 5) {
-        tmem_alloc<kCtaGroup>(smem_u32(tmem_slot), kTmemCols);
+        tmem_alloc<kCtaGroup>(smem_u32(tmem_slot), C::kTmemCols);
         tmem_relinquish<kCtaGroup>();
     }
     tc_fence_before();
@@ -190,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 4) {
         // ---------------- producer ----------------
+        const uint32_t a_bytes = p.a_box_rows > 0 ? static_cast<uint32_t>(p.a_box_rows) * kBlockK * 2u : C::kABytes;
         int stage = 0;
         uint32_t phase = 0;
         int issued = 0;
@@ -199,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int tm, tn, kb0, kb1;
             work_coords(t, p, &tm, &tn, &kb0, &kb1);
             const int row0 = tm * C::kTileM + static_cast<int>(rank) * kBlockM;
-            const int col0 = tn * kBlockN + static_cast<int>(rank) * C::kBCols;
+            const int col0 = tn * kBN + static_cast<int>(rank) * C::kBCols;
             for (int kb = kb0; kb < kb1; ++kb) {
                 if (!mbar_wait_warp(empty_bar(stage), phase ^ 1u, kFaultProducerWait, abort_flag)) {
                     ok = false;
@@ -209,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_dst = base + stage * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     if constexpr (kCtaGroup == 1) {
-                        mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
+                        mbar_arrive_expect_tx(full_bar(stage), a_bytes + C::kBBytes);
                         tma_load_2d(a_dst, &map_a, full_bar(stage), kb * kBlockK, row0);
 #pragma unroll
                         for (int j = 0; j < C::kBCols / 64; ++j)
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 int tm, tn, kb0, kb1;
                 work_coords(t, p, &tm, &tn, &kb0, &kb1);
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBlockN);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_warp(full_bar(stage), phase, kFaultMmaWait, abort_flag)) {
                         ok = false;
@@ -315,16 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const long long row =
                 static_cast<long long>(tm) * C::kTileM + rank * kBlockM + warp * 32 + lane;
-            const int col_base = tn * kBlockN;
+            const int col_base = tn * kBN;
             const bool row_ok = row < p.m;
             const bool split = kStats != kEpiSplitCluster && p.k_splits > 1;
             float* crow = split ? p.ws + (static_cast<long long>(t % p.k_splits) * p.m + row) * p.n
                                 : p.c + row * p.ldc;
             const bool vec4 = split || p.c_vec4;
-            const uint32_t t_addr = tmem_base + ((warp * 32u) << 16) + static_cast<uint32_t>(acc * kBlockN);
+            const uint32_t t_addr = tmem_base + ((warp * 32u) << 16) + static_cast<uint32_t>(acc * kBN);
             float gmax[16], gsum[16];
 #pragma unroll
-            for (int chunk = 0; chunk < kBlockN / 32; ++chunk) {
+            for (int chunk = 0; chunk < kBN / 32; ++chunk) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_addr + chunk * 32, r);
                 tmem_wait_ld();
@@ -358,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // Partial rows stay in this CTA's shared memory (the pipeline stages
                     // are idle: every load of the CTA's one work unit has been consumed).
                     if (row_ok) {
-                        float* prow = reinterpret_cast<float*>(smem) + (warp * 32 + lane) * kRedStride + chunk * 32;
+                        float* prow = reinterpret_cast<float*>(smem) + (warp * 32 + lane) * C::kRedStride + chunk * 32;
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
                             *reinterpret_cast<float4*>(prow + 4 * q) =
@@ -406,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float m_t = pairwise16<OpMaxG>(gmax, groups);
                 float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int chunk = 0; chunk < kBlockN / 32; ++chunk) {
+                for (int chunk = 0; chunk < kBN / 32; ++chunk) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_addr + chunk * 32, r);
                     tmem_wait_ld();
@@ -456,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kCtaGroup == 2) cluster_sync();
     if constexpr (kStats == kEpiSplitCluster) {
         static_assert(kCtaGroup == 1, "the in-cluster split-K reduction runs on single-CTA tiles");
-        static_assert(kBlockM * kRedStride * 4 <= Cfg<kCtaGroup>::kStages * Cfg<kCtaGroup>::kStageBytes,
+        static_assert(kBlockM * C::kRedStride * 4 <= C::kStages * C::kStageBytes,
                       "partial tile larger than the pipeline stages");
         // Every CTA reaches both barriers, also after a timed-out wait (its partial is
         // then not used: the fault is recorded and the call reports it).
@@ -464,14 +471,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tm, tn, kb0, kb1;
         work_coords(static_cast<int>(blockIdx.x), p, &tm, &tn, &kb0, &kb1);
         const int rows = min(kBlockM, p.m - tm * kBlockM);
-        const int quads_per_row = min(kBlockN, p.n - tn * kBlockN) / 4;
+        const int quads_per_row = min(kBN, p.n - tn * kBN) / 4;
         const int quads = rows * quads_per_row;
         const int my = static_cast<int>(cluster_ctarank());
         const int q_end = quads * (my + 1) / p.k_splits;
         for (int q = quads * my / p.k_splits + static_cast<int>(threadIdx.x); q < q_end; q += kThreads) {
             const int r = q / quads_per_row;
             const int c4 = (q - r * quads_per_row) * 4;
-            const uint32_t local = base + static_cast<uint32_t>((r * kRedStride + c4) * 4);
+            const uint32_t local = base + static_cast<uint32_t>((r * C::kRedStride + c4) * 4);
             // Split order, as splitk_reduce_kernel: bit-identical results.
             float4 acc = ld_shared_cluster_f4(mapa_shared(local, 0));
             for (int sp = 1; sp < p.k_splits; ++sp) {
@@ -481,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 acc.z += v.z;
                 acc.w += v.w;
             }
-            float* dst = p.c + (static_cast<long long>(tm) * kBlockM + r) * p.ldc + tn * kBlockN + c4;
+            float* dst = p.c + (static_cast<long long>(tm) * kBlockM + r) * p.ldc + tn * kBN + c4;
             if (p.c_vec4) {
                 *reinterpret_cast<float4*>(dst) = acc;
             } else {
@@ -495,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (warp == 5) {
         tc_fence_after();
-        tmem_dealloc<kCtaGroup>(tmem_base, kTmemCols);
+        tmem_dealloc<kCtaGroup>(tmem_base, C::kTmemCols);
     }
 }
 

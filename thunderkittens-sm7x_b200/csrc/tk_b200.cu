@@ -116,11 +116,11 @@ cudaError_t rowops(const float* tiles, size_t n_tiles, float* sum_out, float* ma
 
 int g_gemm_cta_group_override = 0;  // 0 = choose by problem size
 
-template <int kCtaGroup, int kStats>
+template <int kCtaGroup, int kStats, int kBN = tk::gemm::kBlockN>
 cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
                                int device, int sm_count, cudaStream_t stream) {
-    using Cfg = tk::gemm::Cfg<kCtaGroup>;
-    auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kStats>;
+    using Cfg = tk::gemm::Cfg<kCtaGroup, kBN>;
+    auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kStats, kBN>;
     static bool configured[tk::host::kMaxDevices] = {};
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -149,10 +149,11 @@ int g_gemm_splitk_mode = 0;  // 0 = in-cluster reduction where it fits, 1 = alwa
 
 // Split-K with the reduction inside the kernel: grid = every work unit, clusters
 // of k_splits CTAs (one output tile each).
+template <int kBN>
 cudaError_t launch_gemm_split_cluster(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
-                                      int device, cudaStream_t stream) {
-    using Cfg = tk::gemm::Cfg<1>;
-    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster>;
+                                      cudaStream_t stream) {
+    using Cfg = tk::gemm::Cfg<1, kBN>;
+    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster, kBN>;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(p.num_tiles));
     cfg.blockDim = dim3(tk::gemm::kThreads);
@@ -168,15 +169,17 @@ cudaError_t launch_gemm_split_cluster(const CUtensorMap& ma, const CUtensorMap& 
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
 }
 
-// How many clusters of `splits` CTAs of the in-cluster split-K kernel can be
-// resident at once on `device` (cached; 0 when the query fails).
+// How many clusters of `splits` CTAs of the in-cluster split-K kernel with
+// kBN-column tiles can be resident at once on `device` (cached; 0 when the query
+// fails). Also sets the kernel's shared-memory limit, which its launch needs.
+template <int kBN>
 int split_cluster_capacity(int device, int splits) {
     static std::atomic<int> cache[tk::host::kMaxDevices][9];
     static std::atomic<bool> configured[tk::host::kMaxDevices];
     int v = cache[device][splits].load(std::memory_order_acquire);
     if (v != 0) return v < 0 ? 0 : v;
-    using Cfg = tk::gemm::Cfg<1>;
-    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster>;
+    using Cfg = tk::gemm::Cfg<1, kBN>;
+    auto kernel = tk::gemm::gemm_kernel<1, tk::gemm::kEpiSplitCluster, kBN>;
     if (!configured[device].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
             cudaSuccess) {
@@ -203,6 +206,52 @@ int split_cluster_capacity(int device, int splits) {
     }
     cache[device][splits].store(clusters > 0 ? clusters : -1, std::memory_order_release);
     return clusters;
+}
+
+// Tiling of a GEMM on single-CTA or CTA-pair tiles: tile width, K splits.
+struct GemmPlan {
+    int bn = tk::gemm::kBlockN;  // columns per tile: 256, or 128 for small-M split-K
+    int n_tiles = 0;
+    long long tiles = 0;
+    int k_splits = 1, kb_per_split = 0;
+    bool cluster_fits = false;  // every tile's cluster of k_splits CTAs is resident at once
+};
+
+// Splits K when the output has too few tiles to occupy the GPU (decode-shaped
+// problems): at least 4 K blocks per split, partials at most 64 MiB. On single-CTA
+// tiles the split count is then lowered, if needed, to the largest one (at most 8:
+// the portable cluster size) whose tile clusters can all be resident at once, so
+// the splits of a tile can reduce inside their cluster. The plan does not depend
+// on how the splits are reduced.
+template <int kBN>
+GemmPlan plan_gemm(long long m_tiles, long long m, long long n, int k_blocks, bool may_split, int cta_group,
+                   int sm_count, int device) {
+    GemmPlan g;
+    g.bn = kBN;
+    g.n_tiles = static_cast<int>((n + kBN - 1) / kBN);
+    g.tiles = m_tiles * g.n_tiles;
+    g.kb_per_split = k_blocks;
+    if (may_split && g.tiles < sm_count / 2 && k_blocks >= 8) {
+        int splits = static_cast<int>(sm_count / g.tiles);
+        if (splits > k_blocks / 4) splits = k_blocks / 4;
+        while (splits > 1 && static_cast<long long>(splits) * m * n * 4 > (64LL << 20)) --splits;
+        if (splits > 1) {
+            g.kb_per_split = (k_blocks + splits - 1) / splits;
+            g.k_splits = (k_blocks + g.kb_per_split - 1) / g.kb_per_split;
+        }
+    }
+    if (g.k_splits > 1 && cta_group == 1) {
+        for (int s = g.k_splits < 8 ? g.k_splits : 8; s >= 2 && !g.cluster_fits; --s) {
+            const int kb_per = (k_blocks + s - 1) / s;
+            const int splits = (k_blocks + kb_per - 1) / kb_per;
+            if (splits >= 2 && g.tiles <= split_cluster_capacity<kBN>(device, splits)) {
+                g.kb_per_split = kb_per;
+                g.k_splits = splits;
+                g.cluster_fits = true;
+            }
+        }
+    }
+    return g;
 }
 
 // Destinations of the multi-GPU gathered GEMM: rank `rank` of `count` writes its m
@@ -280,10 +329,32 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
     }
 
+    const int tile_m = tk::gemm::kBlockM * cta_group;
+    const long long m_tiles = (m + tile_m - 1) / tile_m;
+    const int k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
+    const bool may_split = !stats && !gathered;
+    GemmPlan plan = plan_gemm<256>(m_tiles, m, n, k_blocks, may_split, cta_group, sm_count, device);
+    // Small split-K problems that leave more than half of the SMs idle take
+    // 128-column tiles when these put more CTAs to work. Measured per call, back to
+    // back: 512^3 14.5 -> 11.5 us (16 -> 32 CTAs), 48 x 784 x 2048 10.3 -> 8.8 us
+    // (32 -> 56 CTAs); 16 x 4096 x 4096 (96 CTAs on 256-column tiles) was slower
+    // on 128 CTAs of 128 columns, 11.8 vs 11.3 us.
+    if (plan.cluster_fits && plan.tiles * plan.k_splits <= sm_count / 2) {
+        const GemmPlan narrow = plan_gemm<128>(m_tiles, m, n, k_blocks, may_split, cta_group, sm_count, device);
+        if (narrow.cluster_fits && narrow.tiles * narrow.k_splits > plan.tiles * plan.k_splits) plan = narrow;
+    }
+    if (plan.tiles > INT_MAX / (plan.k_splits > 0 ? plan.k_splits : 1)) {
+        if (a_tmp) cudaFreeAsync(a_tmp, stream);
+        if (b_tmp) cudaFreeAsync(b_tmp, stream);
+        return cudaErrorInvalidValue;
+    }
+    // When all of M fits one single-CTA tile, A boxes hold only its rows.
+    const uint32_t a_rows = (cta_group == 1 && m < tk::gemm::kBlockM) ? static_cast<uint32_t>(m) : 128u;
+
     CUtensorMap ma, mb;
     const uint64_t a_dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
     const uint64_t a_strides[1] = {static_cast<uint64_t>(lda_use) * 2};
-    const uint32_t a_box[2] = {64, 128};
+    const uint32_t a_box[2] = {64, a_rows};
     const uint64_t b_dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
     const uint64_t b_strides[1] = {static_cast<uint64_t>(ldb_use) * 2};
     const uint32_t b_box[2] = {64, 64};
@@ -306,47 +377,17 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         for (int r = 0; r < gather.count; ++r) p.dst[r] = gather.bufs[r];
         p.dst_row0 = static_cast<long long>(gather.rank) * m;
     }
-    const int tile_m = tk::gemm::kBlockM * cta_group;
-    p.m_tiles = (m + tile_m - 1) / tile_m;
-    p.n_tiles = (n + tk::gemm::kBlockN - 1) / tk::gemm::kBlockN;
-    p.k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
-    const long long tiles = static_cast<long long>(p.m_tiles) * p.n_tiles;
-    if (tiles > INT_MAX) {
-        if (a_tmp) cudaFreeAsync(a_tmp, stream);
-        if (b_tmp) cudaFreeAsync(b_tmp, stream);
-        return cudaErrorInvalidValue;
-    }
-    // Split K when the output has too few tiles to occupy the GPU (decode-shaped
-    // problems): at least 4 K blocks per split, partials at most 64 MiB.
-    p.k_splits = 1;
-    p.kb_per_split = p.k_blocks;
-    if (!stats && !gathered && tiles < sm_count / 2 && p.k_blocks >= 8) {
-        int splits = static_cast<int>(sm_count / tiles);
-        if (splits > p.k_blocks / 4) splits = p.k_blocks / 4;
-        while (splits > 1 && static_cast<long long>(splits) * m * n * 4 > (64LL << 20)) --splits;
-        if (splits > 1) {
-            p.kb_per_split = (p.k_blocks + splits - 1) / splits;
-            p.k_splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;
-        }
-    }
-    // On single-CTA tiles the split count is lowered, if needed, to the largest one
-    // (at most 8: the portable cluster size) whose tile clusters can all be resident
-    // at once; the splits of a tile then reduce inside their cluster. Otherwise the
-    // partials go through scratch to splitk_reduce_kernel. Both add the same splits
-    // in the same order, so the reduction mode does not change the results.
-    bool cluster_fits = false;
-    if (p.k_splits > 1 && cta_group == 1) {
-        for (int s = p.k_splits < 8 ? p.k_splits : 8; s >= 2 && !cluster_fits; --s) {
-            const int kb_per = (p.k_blocks + s - 1) / s;
-            const int splits = (p.k_blocks + kb_per - 1) / kb_per;
-            if (splits >= 2 && tiles <= split_cluster_capacity(device, splits)) {
-                p.kb_per_split = kb_per;
-                p.k_splits = splits;
-                cluster_fits = true;
-            }
-        }
-    }
-    const bool cluster_reduce = cluster_fits && g_gemm_splitk_mode == 0;
+    p.a_box_rows = a_rows < 128u ? static_cast<int>(a_rows) : 0;
+    p.m_tiles = static_cast<int>(m_tiles);
+    p.n_tiles = plan.n_tiles;
+    p.k_blocks = k_blocks;
+    p.k_splits = plan.k_splits;
+    p.kb_per_split = plan.kb_per_split;
+    const long long tiles = plan.tiles;
+    const bool narrow = plan.bn == 128;
+    // Both reductions add the same splits in the same order: the results do not
+    // depend on the mode.
+    const bool cluster_reduce = plan.cluster_fits && g_gemm_splitk_mode == 0;
     p.num_tiles = static_cast<int>(tiles) * p.k_splits;
     p.ws = nullptr;
     if (p.k_splits > 1 && !cluster_reduce) {
@@ -376,7 +417,10 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     using tk::gemm::kStatsSoftmax;
     using tk::gemm::kEpiGather;
     if (cluster_reduce) {
-        err = launch_gemm_split_cluster(ma, mb, p, device, stream);
+        err = narrow ? launch_gemm_split_cluster<128>(ma, mb, p, stream)
+                     : launch_gemm_split_cluster<256>(ma, mb, p, stream);
+    } else if (narrow) {
+        err = launch_gemm_kernel<1, kStatsNone, 128>(ma, mb, p, device, sm_count, stream);
     } else if (cta_group == 2) {
         err = gathered ? launch_gemm_kernel<2, kEpiGather>(ma, mb, p, device, sm_count, stream)
               : softmax ? launch_gemm_kernel<2, kStatsSoftmax>(ma, mb, p, device, sm_count, stream)
