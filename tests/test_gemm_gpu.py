@@ -191,7 +191,7 @@ def test_split_k_cluster_reduction_matches_kernel(m, n, k, ldc):
     """The in-cluster split-K reduction (the K splits of a tile form a cluster and sum
     their partials over distributed shared memory) and the separate reduction kernel
     add the same partials in the same order: bit-identical C, padding untouched. The
-    shapes cover 256- and 128-column tiles and A boxes of fewer than 128 rows."""
+    shapes cover 256- and 128-column tiles."""
     a, b = oracle.gen_gemm_normal(7, 0.02, m, n, k, k, n)
     sentinel = np.float32(-5.0)
     prev = tk_b200.set_gemm_splitk_reduce(1)

@@ -71,10 +71,6 @@ struct Params {
     // sums the splits in order into C (deterministic). k_splits == 1 writes C directly.
     int k_splits, kb_per_split;
     float* ws;
-    // Rows of A per TMA box (single-CTA tiles; 0 = kBlockM). When all of M fits one
-    // tile, only round_up(M, 16) rows are fetched: the MMA's other rows read stale
-    // shared memory and only produce accumulator rows that are never stored.
-    int a_box_rows;
     // Fused row statistics: per-(row, n-tile) partials, then a finishing pass.
     float* partial;     // [m][n_tiles][2] (max, sum), or null
     // kEpiGather: row r of this GEMM goes to row dst_row0 + r of every dst[0..n_dst)
@@ -196,7 +192,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 4) {
         // ---------------- producer ----------------
-        const uint32_t a_bytes = p.a_box_rows > 0 ? static_cast<uint32_t>(p.a_box_rows) * kBlockK * 2u : C::kABytes;
         int stage = 0;
         uint32_t phase = 0;
         int issued = 0;
@@ -216,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_dst = base + stage * C::kStageBytes;
                     const uint32_t b_dst = a_dst + C::kABytes;
                     if constexpr (kCtaGroup == 1) {
-                        mbar_arrive_expect_tx(full_bar(stage), a_bytes + C::kBBytes);
+                        mbar_arrive_expect_tx(full_bar(stage), C::kStageBytes);
                         tma_load_2d(a_dst, &map_a, full_bar(stage), kb * kBlockK, row0);
 #pragma unroll
                         for (int j = 0; j < C::kBCols / 64; ++j)

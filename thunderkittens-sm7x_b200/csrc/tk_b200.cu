@@ -348,13 +348,11 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         if (b_tmp) cudaFreeAsync(b_tmp, stream);
         return cudaErrorInvalidValue;
     }
-    // When all of M fits one single-CTA tile, A boxes hold only its rows.
-    const uint32_t a_rows = (cta_group == 1 && m < tk::gemm::kBlockM) ? static_cast<uint32_t>(m) : 128u;
 
     CUtensorMap ma, mb;
     const uint64_t a_dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
     const uint64_t a_strides[1] = {static_cast<uint64_t>(lda_use) * 2};
-    const uint32_t a_box[2] = {64, a_rows};
+    const uint32_t a_box[2] = {64, 128};
     const uint64_t b_dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
     const uint64_t b_strides[1] = {static_cast<uint64_t>(ldb_use) * 2};
     const uint32_t b_box[2] = {64, 64};
@@ -377,7 +375,6 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         for (int r = 0; r < gather.count; ++r) p.dst[r] = gather.bufs[r];
         p.dst_row0 = static_cast<long long>(gather.rank) * m;
     }
-    p.a_box_rows = a_rows < 128u ? static_cast<int>(a_rows) : 0;
     p.m_tiles = static_cast<int>(m_tiles);
     p.n_tiles = plan.n_tiles;
     p.k_blocks = k_blocks;
