@@ -114,7 +114,8 @@ cudaError_t rowops(const float* tiles, size_t n_tiles, float* sum_out, float* ma
 // GEMM
 // ---------------------------------------------------------------------------
 
-int g_gemm_cta_group_override = 0;  // 0 = choose by problem size
+// Process-wide tuning knobs, read by every call (possibly from several host threads).
+std::atomic<int> g_gemm_cta_group_override{0};  // 0 = choose by problem size
 
 template <int kCtaGroup, int kStats, int kBN = tk::gemm::kBlockN>
 cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, const tk::gemm::Params& p,
@@ -145,7 +146,7 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
 }
 
-int g_gemm_splitk_mode = 0;  // 0 = in-cluster reduction where it fits, 1 = always the separate kernel
+std::atomic<int> g_gemm_splitk_mode{0};  // 0 = in-cluster reduction where it fits, 1 = always the separate kernel
 
 // Split-K with the reduction inside the kernel: grid = every work unit, clusters
 // of k_splits CTAs (one output tile each).
@@ -323,7 +324,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
         ldb_use = n;
     }
 
-    int cta_group = g_gemm_cta_group_override;
+    int cta_group = g_gemm_cta_group_override.load(std::memory_order_relaxed);
     if (cta_group == 0) {
         const long long big_tiles = ((m + 255LL) / 256) * ((n + 255LL) / 256);
         cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
@@ -384,7 +385,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     const bool narrow = plan.bn == 128;
     // Both reductions add the same splits in the same order: the results do not
     // depend on the mode.
-    const bool cluster_reduce = plan.cluster_fits && g_gemm_splitk_mode == 0;
+    const bool cluster_reduce = plan.cluster_fits && g_gemm_splitk_mode.load(std::memory_order_relaxed) == 0;
     p.num_tiles = static_cast<int>(tiles) * p.k_splits;
     p.ws = nullptr;
     if (p.k_splits > 1 && !cluster_reduce) {
@@ -513,7 +514,7 @@ cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, c
     err = noalloc_scratch(device, &scratch);
     if (err != cudaSuccess) return err;
 
-    int cta_group = g_gemm_cta_group_override;
+    int cta_group = g_gemm_cta_group_override.load(std::memory_order_relaxed);
     if (cta_group == 0) {
         const long long big_tiles = ((m + 255LL) / 256) * ((n + 255LL) / 256);
         cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
@@ -631,15 +632,13 @@ cudaError_t tk_ipc_free(void* ptr) {
 }
 
 int tk_gemm_set_cta_group(int cta_group) {
-    const int prev = g_gemm_cta_group_override;
-    if (cta_group >= 0 && cta_group <= 2) g_gemm_cta_group_override = cta_group;
-    return prev;
+    if (cta_group < 0 || cta_group > 2) return g_gemm_cta_group_override.load();
+    return g_gemm_cta_group_override.exchange(cta_group);
 }
 
 int tk_gemm_set_splitk_reduce(int mode) {
-    const int prev = g_gemm_splitk_mode;
-    if (mode == 0 || mode == 1) g_gemm_splitk_mode = mode;
-    return prev;
+    if (mode != 0 && mode != 1) return g_gemm_splitk_mode.load();
+    return g_gemm_splitk_mode.exchange(mode);
 }
 
 cudaError_t tk_tile_row_sum_f32(const float* tiles, size_t n_tiles, float* out, cudaStream_t stream) {
