@@ -22,6 +22,12 @@
 //
 // The persistent grid walks output tiles in groups of kGroupM tile-rows so that
 // the CTAs resident at one time share A row-blocks and B column-blocks in L2.
+//
+// Output shapes with too few tiles to fill the GPU split K: one work unit per
+// (tile, K split). The splits of a tile either form a thread-block cluster and sum
+// their partials over distributed shared memory (kEpiSplitCluster, one launch), or
+// write partials that splitk_reduce_kernel sums; both in split order. Small such
+// problems use 128-column tiles (kBN = 128: MMA N = 128, 256 TMEM columns).
 #pragma once
 
 #include "tk_ptx.cuh"
@@ -132,7 +138,6 @@ enum Stats : int {
     // of the tile over all splits in split order (distributed shared memory) into C.
     kEpiSplitCluster = 4,
 };
-
 
 template <int kCtaGroup, int kStats, int kBN = kBlockN>
 __global__ void __launch_bounds__(kThreads, 1)
