@@ -229,9 +229,20 @@ TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, co
 
 /* Every wait inside the library's kernels is bounded. A kernel that gives up on
  * a wait records a nonzero code in a per-device status word and returns
- * instead of hanging. This reads (and with clear != 0 resets) that word for the
- * current device; it synchronises the device. */
+ * instead of hanging; its outputs are then incomplete. This reads (and with
+ * clear != 0 resets) that word for the current device; it synchronises the
+ * device. While the word is nonzero, the finishing passes of the row-statistics
+ * and row-softmax GEMMs write NaN instead of results built from per-tile
+ * partials that a stopped GEMM may not have written. */
 TK_API cudaError_t tk_device_status(uint32_t* status, int clear);
+
+/* No counterpart in the reference (diagnostic). Bytes that the library's private
+ * stream-ordered scratch pool on `device` has reserved from the driver
+ * (*reserved) and currently hands out to allocations not yet freed (*used). The
+ * pool is created by the first call on that device that needs scratch (repacked
+ * operands, split-K partials, row-statistics pairs, the attention work counter);
+ * until then both are 0. Device ordinal out of range: cudaErrorInvalidDevice. */
+TK_API cudaError_t tk_scratch_pool_bytes(int device, uint64_t* reserved, uint64_t* used);
 
 /* Version of this C ABI (major * 100 + minor). */
 TK_API int tk_abi_version(void);

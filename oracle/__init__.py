@@ -39,11 +39,19 @@ _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 
 
+def ref_root() -> str:
+    """The ThunderKittens-SM7x source tree: $REF_ROOT, else a `reference` directory
+    beside this repository's checkout (it is only read by the `ref` and `legacy`
+    build recipes, never at test or bench time)."""
+    return os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
 def build(ref: bool = False) -> None:
     """Compile the oracle (and, if asked and the reference tree exists, _ref)."""
     targets = ["all"]
-    if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference")):
-        targets += ["ref", "legacy"]
+    root = ref_root()
+    if ref and os.path.isdir(root):
+        targets += ["ref", "legacy", f"REF_ROOT={root}"]
     subprocess.run(["make", "-s", "-C", HERE, *targets], check=True)
 
 

@@ -34,7 +34,7 @@ def test_library_exports_every_declared_symbol():
     lib = C.CDLL(tk_b200.LIB_PATH)
     for name in declared_symbols():
         assert hasattr(lib, name), name
-    assert tk_b200.lib().tk_abi_version() == 100
+    assert tk_b200.lib().tk_abi_version() == 101
 
 
 def test_library_exports_nothing_undeclared():

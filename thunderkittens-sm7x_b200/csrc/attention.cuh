@@ -31,6 +31,7 @@
 // (512*2^-23 + 2^-11 + gamma(2S)) * sum_t |V[t, c]|.
 #pragma once
 
+#include <atomic>
 #include <climits>
 
 #include "tk_host.cuh"
@@ -785,13 +786,15 @@ template <int kDPad>
 cudaError_t launch(const void* q, const void* k, const void* v, const Params& p, int device, int grid,
                    cudaStream_t stream) {
     using Cc = Cfg<kDPad>;
-    static bool configured[host::kMaxDevices] = {};
+    // Per-device shared-memory opt-in, done once; concurrent first calls may both
+    // set the (idempotent) attribute.
+    static std::atomic<bool> configured[host::kMaxDevices];
     auto kernel = attention_kernel<kDPad>;
-    if (!configured[device]) {
+    if (!configured[device].load(std::memory_order_acquire)) {
         cudaError_t e =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cc::kSmemBytes);
         if (e != cudaSuccess) return e;
-        configured[device] = true;
+        configured[device].store(true, std::memory_order_release);
     }
     CUtensorMap mq, mk, mv;
     const uint64_t dims[3] = {static_cast<uint64_t>(p.head_dim), static_cast<uint64_t>(p.seq),

@@ -510,10 +510,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // partials in tile order with the same pairwise rule (binary-counter form: a
 // stack of complete power-of-two blocks, merged right to left at the end, which
 // equals the level-by-level pairing with the odd element carried up).
+//
+// A GEMM that gave up on a bounded wait leaves some partials unwritten; while the
+// status word records such a fault the pass writes NaN instead of combining them.
 __global__ void rowstats_finish_kernel(const float2* partial, int m, int n_tiles, float* row_max,
                                        float* row_sum) {
     const long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (row >= m) return;
+    if (*static_cast<volatile unsigned int*>(&g_tk_status) != 0u) {
+        row_max[row] = __int_as_float(0x7fc00000);
+        row_sum[row] = __int_as_float(0x7fc00000);
+        return;
+    }
     float smax[32], ssum[32];
     int ssize[32];
     int top = 0;
@@ -546,11 +554,13 @@ __global__ void rowstats_finish_kernel(const float2* partial, int m, int n_tiles
 // row: the lanes merge the pairs (row max M, normaliser S = sum s_t exp(m_t - M),
 // a fixed shuffle order, so the result is deterministic), then the warp writes
 // p = exp(c - M) / S over the row. p may be c itself: each element is read before
-// the same lane overwrites it.
+// the same lane overwrites it. While the status word records a fault (a GEMM that
+// gave up on a wait, leaving pairs unwritten) every p is NaN.
 __global__ void __launch_bounds__(256) rowsoftmax_apply_kernel(const float2* partial, int m, int n,
                                                                int n_tiles, const float* c, long long ldc,
                                                                float* p, long long ldp, bool vec4) {
     constexpr float kLog2e = 1.4426950408889634f;
+    const bool faulted = *static_cast<volatile unsigned int*>(&g_tk_status) != 0u;
     const int lane = threadIdx.x & 31;
     const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
     for (long long row = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5); row < m;
@@ -565,7 +575,7 @@ __global__ void __launch_bounds__(256) rowsoftmax_apply_kernel(const float2* par
             total += src[t].y * tk_sm7x::b200::ex2_approx((src[t].x - big) * kLog2e);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-        const float inv = __frcp_rn(total);
+        const float inv = faulted ? __int_as_float(0x7fc00000) : __frcp_rn(total);
         const float* crow = c + row * ldc;
         float* prow = p + row * ldp;
         if (vec4) {

@@ -7,6 +7,7 @@
 
 #include "tk_b200.h"
 
+#include <atomic>
 #include <climits>
 #include <cstdint>
 #include <cstring>
@@ -21,7 +22,7 @@ namespace {
 
 using tk::host::current_device;
 
-constexpr int kAbiVersion = 100;
+constexpr int kAbiVersion = 101;
 
 // ---------------------------------------------------------------------------
 // Tile row operations
@@ -30,16 +31,21 @@ constexpr int kAbiVersion = 100;
 template <int kOps, bool kVec>
 void launch_rowops_typed(const float* tiles, size_t n_tiles, float* s, float* m, float* sm, float* cs,
                          int sm_count, cudaStream_t stream) {
-    static int blocks_per_sm = 0;
+    // Resident blocks per SM, looked up once (several host threads may race to do
+    // it; each stores the same value).
+    static std::atomic<int> cached_blocks_per_sm{0};
+    int blocks_per_sm = cached_blocks_per_sm.load(std::memory_order_acquire);
     if (blocks_per_sm == 0) {
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
                 &occ, tk::rowops::tile_row_ops_kernel<kOps, kVec>, tk::rowops::kThreads, 0) !=
                 cudaSuccess ||
             occ <= 0) {
+            static_cast<void>(cudaGetLastError());
             occ = 4;
         }
         blocks_per_sm = occ;
+        cached_blocks_per_sm.store(occ, std::memory_order_release);
     }
     const size_t tiles_per_block = (tk::rowops::kThreads / 32) * tk::rowops::kTilesPerWarpStep;
     const size_t needed = (n_tiles + tiles_per_block - 1) / tiles_per_block;
@@ -122,12 +128,14 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
                                int device, int sm_count, cudaStream_t stream) {
     using Cfg = tk::gemm::Cfg<kCtaGroup, kBN>;
     auto kernel = tk::gemm::gemm_kernel<kCtaGroup, kStats, kBN>;
-    static bool configured[tk::host::kMaxDevices] = {};
-    if (!configured[device]) {
+    // Per-device shared-memory opt-in, done once; concurrent first calls may both
+    // set the (idempotent) attribute.
+    static std::atomic<bool> configured[tk::host::kMaxDevices];
+    if (!configured[device].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Cfg::kSmemBytes);
         if (e != cudaSuccess) return e;
-        configured[device] = true;
+        configured[device].store(true, std::memory_order_release);
     }
     const int max_clusters = sm_count / kCtaGroup;
     const int clusters = p.num_tiles < max_clusters ? p.num_tiles : max_clusters;
@@ -546,7 +554,10 @@ cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, c
     p.kb_per_split = p.k_blocks;
     p.ws = nullptr;
     // Every (row < m, tile) pair is written by the GEMM epilogue before the
-    // finishing pass reads it, so nothing left by an earlier call is ever used.
+    // finishing pass reads it, so nothing left by an earlier call is used. The one
+    // exception is a GEMM that gave up on a bounded wait: it records a fault in the
+    // status word, and the finishing pass then writes NaN rather than combine pairs
+    // an earlier call may have left.
     p.partial = reinterpret_cast<float*>(scratch);
     err = cta_group == 2 ? launch_gemm_kernel<2, tk::gemm::kStatsMaxSum>(ma, mb, p, device, sm_count, stream)
                          : launch_gemm_kernel<1, tk::gemm::kStatsMaxSum>(ma, mb, p, device, sm_count, stream);
@@ -702,6 +713,12 @@ cudaError_t tk_device_status(uint32_t* status, int clear) {
     }
     *status = value;
     return cudaSuccess;
+}
+
+cudaError_t tk_scratch_pool_bytes(int device, uint64_t* reserved, uint64_t* used) {
+    if (reserved == nullptr || used == nullptr) return cudaErrorInvalidValue;
+    if (device < 0 || device >= tk::host::kMaxDevices) return cudaErrorInvalidDevice;
+    return tk::host::scratch_pool_bytes(device, reserved, used);
 }
 
 int tk_abi_version(void) { return kAbiVersion; }

@@ -101,14 +101,24 @@ inline bool make_map_f16(CUtensorMap* map, const void* base, int rank, const uin
 // Stream-ordered scratch from a private per-device memory pool that keeps its
 // memory (release threshold = max), so repeated calls reuse the same pages instead
 // of mapping and unmapping them around every call. The pool is the library's own;
-// the process's default pool is left untouched.
+// the process's default pool is left untouched. It is created by the first call
+// on a device that needs scratch.
+struct ScratchPools {
+    std::mutex mu;
+    cudaMemPool_t pools[kMaxDevices] = {};
+};
+
+inline ScratchPools& scratch_pools() {
+    static ScratchPools p;
+    return p;
+}
+
 inline cudaError_t scratch_alloc(void** ptr, size_t bytes, int device, cudaStream_t stream) {
-    static cudaMemPool_t pools[kMaxDevices] = {};
-    static std::mutex mu;
+    ScratchPools& sp = scratch_pools();
     cudaMemPool_t pool;
     {
-        std::lock_guard<std::mutex> lock(mu);
-        if (pools[device] == nullptr) {
+        std::lock_guard<std::mutex> lock(sp.mu);
+        if (sp.pools[device] == nullptr) {
             cudaMemPoolProps props{};
             props.allocType = cudaMemAllocationTypePinned;
             props.location.type = cudaMemLocationTypeDevice;
@@ -122,11 +132,24 @@ inline cudaError_t scratch_alloc(void** ptr, size_t bytes, int device, cudaStrea
                 static_cast<void>(cudaMemPoolDestroy(created));
                 return err;
             }
-            pools[device] = created;
+            sp.pools[device] = created;
         }
-        pool = pools[device];
+        pool = sp.pools[device];
     }
     return cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
+}
+
+// Bytes the scratch pool of `device` has reserved from the driver and has handed
+// out to allocations not yet freed (both 0 while no call has created the pool).
+inline cudaError_t scratch_pool_bytes(int device, uint64_t* reserved, uint64_t* used) {
+    ScratchPools& sp = scratch_pools();
+    std::lock_guard<std::mutex> lock(sp.mu);
+    *reserved = 0;
+    *used = 0;
+    if (sp.pools[device] == nullptr) return cudaSuccess;
+    cudaError_t err = cudaMemPoolGetAttribute(sp.pools[device], cudaMemPoolAttrReservedMemCurrent, reserved);
+    if (err != cudaSuccess) return err;
+    return cudaMemPoolGetAttribute(sp.pools[device], cudaMemPoolAttrUsedMemCurrent, used);
 }
 
 inline bool ranges_overlap(const void* a, size_t a_bytes, const void* b, size_t b_bytes) {

@@ -51,6 +51,7 @@ SIGNATURES = {
     "tk_attention_forward_f16": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _F, _I, _VP]),
     "tk_attention_forward_gqa_f16": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tk_device_status": (_I, [C.POINTER(C.c_uint32), _I]),
+    "tk_scratch_pool_bytes": (_I, [_I, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "tk_abi_version": (_I, []),
 }
 
@@ -186,6 +187,13 @@ def device_status(clear: bool = False) -> int:
     v = C.c_uint32()
     _check("tk_device_status", lib().tk_device_status(C.byref(v), 1 if clear else 0))
     return v.value
+
+
+def scratch_pool_bytes(device: int = 0) -> tuple[int, int]:
+    """(reserved, used) bytes of the library's scratch pool on `device`."""
+    reserved, used = C.c_uint64(), C.c_uint64()
+    _check("tk_scratch_pool_bytes", lib().tk_scratch_pool_bytes(device, C.byref(reserved), C.byref(used)))
+    return reserved.value, used.value
 
 
 # ---- torch-level helpers (device tensors in, device tensors out) ---------------------
