@@ -225,6 +225,14 @@ TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, co
                                                 int seq, int head_dim, float scale, int causal,
                                                 cudaStream_t stream);
 
+/* No counterpart in the reference (a tuning switch). Attention with head_dim 128,
+ * more than 128 keys and a positive scale runs on CTA pairs (tcgen05 cta_group::2,
+ * M = 256 tiles) by default; 1 selects the single-CTA kernel for those problems
+ * instead, 0 or 2 the CTA-pair kernel. Both give results inside the same bound.
+ * Returns the previous setting (0 or 1); other values only query it. Process-wide;
+ * every call reads it. */
+TK_API int tk_attention_set_cta_group(int cta_group);
+
 /* ---- status ------------------------------------------------------------------ */
 
 /* Every wait inside the library's kernels is bounded. A kernel that gives up on

@@ -1,8 +1,18 @@
-// Batched host counterparts of ThunderKittens-SM7x include/tk_sm7x/reduce.cuh:43-51.
-// The reference's row_sum / row_max reduce one 16x16 FP32 accumulator held by a
-// warp; here they reduce n_tiles contiguous 16x16 row-major FP32 tiles resident in
-// device memory, with the same balanced column-order tree (bit-identical results;
-// max ties pick the right operand).
+// Row sums and maxima of 16x16 FP32 tiles: ThunderKittens-SM7x
+// include/tk_sm7x/reduce.cuh:43-51, in two forms.
+//
+// Device (CUDA translation units): tk_sm7x::row_sum / row_max(float* dst,
+// const rt_c& src, st<float, 16, 16, row_major>& scratch), the reference's
+// signatures, with rt_c the sm_100a accumulator tile (tile_b200.cuh). Same call
+// contract: all 32 lanes of a warp call convergently, dst holds 16 floats, the
+// call ends with a warp barrier. The scratch tile is accepted for source
+// compatibility and left untouched (the layout needs no shared-memory round trip).
+//
+// Host (batched): tile_row_sum / tile_row_max reduce n_tiles contiguous 16x16
+// row-major FP32 tiles resident in device memory.
+//
+// Both use the reference's balanced column-order tree: bit-identical results, max
+// ties (and signed zeros) pick the right operand.
 #pragma once
 
 #include <cstddef>
@@ -24,3 +34,21 @@ inline cudaError_t tile_row_max(const float* tiles, std::size_t n_tiles, float* 
 }
 
 }  // namespace tk_sm7x
+
+#if defined(__CUDACC__)
+#include "tk_sm7x/tile_b200.cuh"
+
+namespace tk_sm7x {
+
+__device__ __forceinline__ void row_sum(float* dst, const rt_c& src, st<float, 16, 16, row_major>& scratch) {
+    static_cast<void>(scratch);
+    b200::row_sum(dst, src);
+}
+
+__device__ __forceinline__ void row_max(float* dst, const rt_c& src, st<float, 16, 16, row_major>& scratch) {
+    static_cast<void>(scratch);
+    b200::row_max(dst, src);
+}
+
+}  // namespace tk_sm7x
+#endif

@@ -202,4 +202,35 @@ __device__ __forceinline__ tile16 row_softmax_causal(const tile16& t) {
 }
 
 }  // namespace b200
+
+// Reference-named tile types, so that device code written against the reference's
+// warp tile API (include/tk_sm7x/tile.cuh:30-70) keeps its declarations:
+//   st<T, R, C, Layout>  shared-memory tile: R x C elements in `data`, 32-byte aligned
+//                        (the reference's tile.cuh:30-52 type; row- or column-major);
+//   rt_c                 the 16x16 FP32 accumulator tile a warp holds. On sm_100a it
+//                        is b200::tile16 (documented register layout above) instead
+//                        of an SM7x MMA fragment; it is filled by load() from a
+//                        shared or global tile rather than by a warp-level mma().
+struct row_major {};
+struct col_major {};
+
+template <class T, int R, int C, class Layout = row_major>
+struct alignas(32) st {
+    T data[static_cast<size_t>(R) * C];
+};
+
+using rt_c = b200::tile16;
+
+// Shared tile <-> accumulator tile (warp-collective, row-major FP32 tiles).
+__device__ __forceinline__ void load(rt_c& dst, const st<float, 16, 16, row_major>& src) {
+    b200::load(dst, src.data, 16);
+}
+
+__device__ __forceinline__ void store(st<float, 16, 16, row_major>& dst, const rt_c& src) {
+    b200::store(dst.data, 16, src);
+}
+
+__device__ __forceinline__ void zero(rt_c& t) { b200::zero(t); }
+__device__ __forceinline__ void scale(rt_c& t, float factor) { b200::scale(t, factor); }
+
 }  // namespace tk_sm7x

@@ -71,6 +71,38 @@ def test_tile_api_matches_reference_tree_and_batched_kernels(tile_api, ld):
     assert np.array_equal(bits(host(batched["causal"]).reshape(-1)), bits(cs))
 
 
+@pytest.fixture(scope="module")
+def refnames(tmp_path_factory):
+    so = tmp_path_factory.mktemp("refnames") / "librefnames.so"
+    subprocess.run(["nvcc", "-std=c++17", "-O2", "-gencode", "arch=compute_100a,code=sm_100a", "-shared",
+                    "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(HERE, "device_api", "refnames_kernels.cu"), "-o", str(so)], check=True)
+    lib = C.CDLL(str(so))
+    lib.refnames_run.restype = C.c_int
+    lib.refnames_run.argtypes = [C.c_void_p, C.c_int] + [C.c_void_p] * 4
+    return lib
+
+
+def test_reference_named_device_api(refnames):
+    """tk_sm7x::row_sum / row_max / row_softmax / row_softmax_causal called with the
+    reference's device signatures from <tk_sm7x/reduce.cuh> and <tk_sm7x/softmax.cuh>:
+    sums and maxima bit-identical to the reference tree (golden tiles included),
+    probabilities within 512 * 2^-23, causal zeros exact."""
+    g = np.load(os.path.join(HERE, "golden", "row_reduce.npz"))
+    tiles = np.concatenate([g["tiles"], oracle.gen_normal_f32(5, 2.0, 61 * 256).reshape(61, 16, 16)])
+    n = tiles.shape[0]
+    d_in = dev(np.ascontiguousarray(tiles, dtype=np.float32))
+    outs = [torch.full((n * 16,), float("nan"), device="cuda") for _ in range(2)]
+    outs += [torch.full((n * 256,), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    assert refnames.refnames_run(d_in.data_ptr(), n, *[o.data_ptr() for o in outs]) == 0
+    sums, maxs, sm, cs = [host(o) for o in outs]
+    assert np.array_equal(bits(sums), bits(oracle.tile_row_reduce(tiles, "sum").reshape(-1)))
+    assert np.array_equal(bits(maxs), bits(oracle.tile_row_reduce(tiles, "max").reshape(-1)))
+    assert oracle.tile_row_softmax_check(tiles, sm, False)[0] == 0
+    assert oracle.tile_row_softmax_check(tiles, cs, True)[0] == 0
+
+
 def example_tile():
     """A and B of examples/gemm_row_stats.cu:74-80 (numerators / 8, exact in FP16)."""
     r, c = np.meshgrid(np.arange(16), np.arange(16), indexing="ij")

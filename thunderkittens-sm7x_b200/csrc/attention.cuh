@@ -813,6 +813,20 @@ cudaError_t launch(const void* q, const void* k, const void* v, const Params& p,
     return cudaSuccess;
 }
 
+namespace pair {
+// CTA-pair kernel for head_dim 128 (attention_pair.cuh).
+inline cudaError_t launch(const void* q, const void* k, const void* v, float* out, int bh, int heads_q,
+                          int heads_kv, int seq, float scale, int causal, int device, int sm_count,
+                          cudaStream_t stream);
+}  // namespace pair
+
+// Kernel choice for head_dim 128, multi-block, positive-scale problems: 0 = the CTA-pair
+// kernel (default), 1 = the single-CTA kernel. Read by every call.
+inline std::atomic<int>& cta_group_knob() {
+    static std::atomic<int> knob{0};
+    return knob;
+}
+
 inline cudaError_t attention_entry(const void* q, const void* k, const void* v, float* out, int batch,
                                    int heads, int heads_kv, int seq, int head_dim, float scale, int causal,
                                    bool fixed_tile, cudaStream_t stream) {
@@ -883,12 +897,18 @@ inline cudaError_t attention_entry(const void* q, const void* k, const void* v, 
         }
     }
     void* counter = nullptr;
-    if (err == cudaSuccess && p.num_items > grid) {
+    if (err == cudaSuccess && p.num_items > grid && !(head_dim == 128 && seq > kBlockKV && scale > 0.0f &&
+                                                      cta_group_knob().load(std::memory_order_relaxed) != 1)) {
         err = host::scratch_alloc(&counter, sizeof(int), device, stream);
         if (err == cudaSuccess) err = cudaMemsetAsync(counter, 0, sizeof(int), stream);
         p.next_item = static_cast<int*>(counter);
     }
-    if (err == cudaSuccess) {
+    const bool use_pair = head_dim == 128 && seq > kBlockKV && scale > 0.0f &&
+                          cta_group_knob().load(std::memory_order_relaxed) != 1;
+    if (err == cudaSuccess && use_pair) {
+        err = pair::launch(src[0], src[1], src[2], out, p.bh, heads, heads_kv, seq, scale, causal, device, sm_count,
+                           stream);
+    } else if (err == cudaSuccess) {
         err = head_dim == 128 ? launch<128>(src[0], src[1], src[2], p, device, grid, stream)
                               : launch<64>(src[0], src[1], src[2], p, device, grid, stream);
     }

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "attention_pair.cuh"
 #include "gemm.cuh"
 #include "rowops.cuh"
 #include "tk_host.cuh"
@@ -645,6 +646,12 @@ cudaError_t tk_ipc_free(void* ptr) {
 int tk_gemm_set_cta_group(int cta_group) {
     if (cta_group < 0 || cta_group > 2) return g_gemm_cta_group_override.load();
     return g_gemm_cta_group_override.exchange(cta_group);
+}
+
+int tk_attention_set_cta_group(int cta_group) {
+    // 0 and 2: the CTA-pair kernel where it applies; 1: always the single-CTA kernel.
+    if (cta_group < 0 || cta_group > 2) return tk::attn::cta_group_knob().load() == 1 ? 1 : 0;
+    return tk::attn::cta_group_knob().exchange(cta_group == 1 ? 1 : 0) == 1 ? 1 : 0;
 }
 
 int tk_gemm_set_splitk_reduce(int mode) {

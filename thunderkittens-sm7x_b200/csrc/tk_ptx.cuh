@@ -115,6 +115,38 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// Cluster-scope acquire form: for barriers that other CTAs of the cluster arrive on
+// (mbarrier.arrive.release.cluster), so that what those CTAs wrote before arriving
+// is visible to this thread after the wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, unsigned int code,
+                                                  volatile int* abort) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const unsigned long long start = global_ns();
+    for (uint32_t polls = 1;; ++polls) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((polls & 15u) == 0) {
+            if (abort != nullptr && *abort) return false;
+            if (global_ns() - start > kWaitTimeoutNs) {
+                record_fault(code);
+                if (abort != nullptr) *abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
 // Whole-warp form: every lane polls, and the outcome is made warp-uniform so that
 // warp-collective instructions after the wait (tcgen05.ld/st, __syncwarp) are
 // never reached by only part of the warp.
@@ -183,6 +215,29 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, uint3
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
         : "memory");
+}
+
+// 3D tiled load into this CTA's shared memory whose completion is counted on a
+// barrier that may live in the peer CTA of a CTA pair (`cluster_bar` from mapa). No
+// multicast: each CTA fetches its own box.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* map, uint32_t cluster_bar, int x,
+                                                 int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy
+// reads of them (tcgen05.mma operands written with st.shared).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
 }
 
 // ---- tcgen05 -------------------------------------------------------------------
