@@ -6,18 +6,33 @@ replicated), one attention forward over [8, 32, 4096, 128] unmasked and one caus
 (this rank's batch x head shard). value = all FLOPs of all ranks / max-over-ranks
 device time, in TFLOP/s.
 
+The same JSON line also carries, as `configs`, one measurement per other benchmark
+configuration of the path (N = 1): GEMM 256^3, the 1,048,576-tile row ops (each op
+and all four fused), the fused row-statistics and row-softmax GEMMs at 8192^3, the
+padded 16384 x 4096 x 14336 GEMM, the decode-shaped 16 x 4096 x 4096 GEMM and the
+one-tile attention; and at N > 1, as `multi_gpu`, the fixed-size (strong scaling)
+GEMM, attention and row ops split across the ranks, the gathered outputs (GEMM with
+the all-gather fused into its epilogue, or GEMM / attention followed by an NCCL
+all-gather), and the hosts' copy bandwidth with every rank copying at once.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload headline|gemm|attention|rowops] [--gather]
+                    [--workload headline|gemm|attention|rowops] [--gather [fused|nccl]]
+                    [--no-configs] [--no-cpu-baseline]
 
 Timing: K steps between two CUDA events on the launching stream, a barrier and
-torch.cuda.synchronize() on both sides, the max over ranks. Inputs are larger than
-L2 (126 MB), so consecutive steps cannot be served from cache. e2e repeats the
-step through the same C ABI with host buffers: pinned host -> device copies of the
-step's inputs and device -> host copies of its outputs inside the timed region.
+torch.cuda.synchronize() on both sides, the max over ranks. Headline inputs are
+larger than L2 (126 MB); configurations whose inputs fit in L2 (256^3, the decode
+GEMM, the one-tile attention) are timed one call at a time with a 256 MiB buffer
+written between calls. Fractions of the tensor peak use the measured burst bf16
+rate when the timed region lasts under a second, else the sustained one. e2e repeats
+the step through the same C ABI with host buffers: pinned host -> device copies of
+the step's inputs and device -> host copies of its outputs inside the timed region.
 
---impl reference times the reference's CPU implementation of the path (its FP64
-host GEMM oracle compiled from its sources, oracle/_ref; the generalised FP64
-attention oracle) on bounded row samples with all host threads, on rank 0 only.
+--impl reference times the reference's CPU implementation of the path on bounded
+row samples with all host threads, on rank 0 only: its FP64 host GEMM oracle
+compiled from its sources (oracle/_ref, "reference") and the generalised FP64
+attention oracle restated from its one-tile host oracle ("port"); the same samples
+as the `cpu_baseline` leg of our arm.
 """
 
 from __future__ import annotations
@@ -59,6 +74,13 @@ def load_peaks():
             p = json.load(f)
         return p, "measured"
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def tensor_peak(peaks, timed_seconds):
+    """(peak TFLOP/s, key): the burst cuBLAS rate for a timed region under a second
+    (the clock has not yet settled under the power cap), the sustained one above."""
+    key = "bf16_tflops" if timed_seconds < 1.0 else "bf16_tflops_sustained"
+    return peaks.get(key, FALLBACK_PEAKS[key]), key
 
 
 def load_traffic():
@@ -224,6 +246,15 @@ class Workload:
             self.h2d += [self.tiles]
             self.d2h += [self.rs, self.rm, self.sm, self.cs]
 
+    @property
+    def call_meta(self):
+        return self._meta
+
+    def freeze(self):
+        """Records (name, work) of the step's calls and its launches per step."""
+        self._meta = [(c[0], c[2]) for c in self.calls]
+        self.launches_per_step = sum(c[3] for c in self.calls)
+
     def step(self, events=None):
         for i, (name, fn, _, _) in enumerate(self.calls):
             if events is not None:
@@ -239,6 +270,7 @@ def run_ours(args, rank, world, local):
     import torch
     fused = args.gather == "fused"
     wl = Workload(args.workload, rank, world, args.row_tiles, fused_gather=fused)
+    wl.freeze()
     for _ in range(args.warmup):
         wl.step()
     torch.cuda.synchronize()
@@ -276,6 +308,7 @@ def run_ours(args, rank, world, local):
     # host->device copy of step i+1 and the device->host copy of step i-1 (the PCIe
     # directions are independent), as a pipelined host application would run.
     wl2 = Workload(args.workload, rank, world, args.row_tiles, fused_gather=fused)
+    wl2.freeze()
     sets = [wl, wl2]
     # One pinned host copy of the inputs and one of the outputs serve both device
     # sets: copies in one direction are serialised on their stream.
@@ -421,26 +454,369 @@ def cpu_sample_attention(threads: int, rows_per_thread: int, causal: bool):
     return flops, dt, f"{rows} query rows x 4096 keys x 128 (FP64 attention, P rounded to FP16)"
 
 
-def cpu_baseline(threads: int, workload: str, gemm_rows: int = 32, attn_rows: int = 1024):
-    """Returns (TFLOP/s over the sampled work, kind, description, CPU seconds) for the
-    step's FLOP mix. The defaults give about 10 s of CPU work."""
+# Rows per host thread of the CPU samples, shared by the cpu_baseline leg of our arm
+# and every step of the reference arm (the same sample in both).
+CPU_GEMM_ROWS, CPU_ATTN_ROWS = 4, 128
+
+
+def cpu_baseline(threads: int, workload: str, gemm_rows: int = CPU_GEMM_ROWS, attn_rows: int = CPU_ATTN_ROWS):
+    """Returns (TFLOP/s over the sampled work, kind, description, seconds, legs) for the
+    step's FLOP mix: legs maps each sampled kernel to "reference" (the reference's own
+    host code, oracle/_ref) or "port" (the restated oracle); kind is "reference" only
+    when every leg is."""
     parts = []
-    kind = "port"
+    legs = {}
     if workload in ("headline", "gemm"):
-        f, dt, kind, desc = cpu_sample_gemm(threads, rows_per_thread=gemm_rows)
+        f, dt, kind_g, desc = cpu_sample_gemm(threads, rows_per_thread=gemm_rows)
         parts.append((f, dt, desc))
+        legs["gemm"] = kind_g
     if workload in ("headline", "attention"):
         f, dt, desc = cpu_sample_attention(threads, min(attn_rows, ATT_S), False)
         parts.append((f, dt, desc))
+        legs["attention"] = "port"  # the reference's host attention oracle is fixed at 16 x 16
     if not parts:
         return None
+    kind = "reference" if all(v == "reference" for v in legs.values()) else "port"
     # Time the sampled work of each kernel and scale to the step's FLOP mix.
     step_mix = {"headline": [gemm_flops(), attn_flops(False) + attn_flops(True)],
                 "gemm": [gemm_flops()], "attention": [attn_flops(False) + attn_flops(True)]}[workload]
     step_seconds = sum(mix / (f / dt) for mix, (f, dt, _) in zip(step_mix, parts))
     tflops = sum(step_mix) / step_seconds / 1e12
     sample = "; ".join(d for _, _, d in parts)
-    return tflops, kind, sample, sum(dt for _, dt, _ in parts)
+    return tflops, kind, sample, sum(dt for _, dt, _ in parts), legs
+
+
+# ---------------------------------------------------------------------------------
+# Per-configuration measurements (single GPU) and multi-GPU components
+# ---------------------------------------------------------------------------------
+
+class L2Flush:
+    """A 256 MiB device buffer (twice the 126 MB L2) written between timed calls whose
+    inputs would otherwise stay in L2."""
+
+    def __init__(self):
+        import torch
+        self.buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def time_calls(fn, iters, flush=None, warmup=3):
+    """Median and minimum device time (ms) of `fn()` over `iters` calls, each between
+    CUDA events on the current stream; `flush` (if given) runs before every call,
+    outside the events. fn returns a cudaError code (0 = success)."""
+    import torch
+    for _ in range(warmup):
+        if flush:
+            flush()
+        code = fn()
+        if code != 0:
+            raise RuntimeError(f"call failed with cudaError {code}")
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for e0, e1 in evs:
+        if flush:
+            flush()
+        e0.record()
+        fn()
+        e1.record()
+    torch.cuda.synchronize()
+    ts = sorted(e0.elapsed_time(e1) for e0, e1 in evs)
+    return ts[len(ts) // 2], ts[0]
+
+
+def run_configs(peaks, traffic, iters=20):
+    """One entry per benchmark configuration other than the headline step (per GPU).
+    Work per call and the bound come from the configuration's algorithmic FLOPs or
+    bytes; frac is against the measured burst bf16 rate (tensor-bound calls, each
+    timed alone) or the measured HBM copy bandwidth (HBM-bound calls)."""
+    import torch
+    import tk_b200
+    gen = torch.Generator(device="cuda")
+    flush = L2Flush()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    burst = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    out = {}
+
+    def tensor_entry(ms, flop, extra=None):
+        rate = flop / (ms / 1e3) / 1e12
+        e = {"ms": round(ms, 4), "TFLOP/s": round(rate, 1), "frac": round(rate / burst, 4), "bound": "tensor",
+             "peak": f"measured bf16_tflops {burst}"}
+        e.update(extra or {})
+        return e
+
+    def hbm_entry(ms, nbytes, extra=None):
+        rate = nbytes / (ms / 1e3) / 1e9
+        e = {"ms": round(ms, 4), "GB/s": round(rate, 1), "frac": round(rate / hbm, 4), "bound": "hbm",
+             "bytes": int(nbytes), "peak": f"measured hbm_gbs {hbm}"}
+        e.update(extra or {})
+        return e
+
+    # cfg1: GEMM 256^3 (U[-1, 1], seed 0), lda = ldb = ldc = 256: a latency-bound call.
+    gen.manual_seed(0)
+    a = (torch.rand(256, 256, device="cuda", generator=gen) * 2 - 1).half()
+    b = (torch.rand(256, 256, device="cuda", generator=gen) * 2 - 1).half()
+    c = torch.empty(256, 256, device="cuda")
+    med, best = time_calls(lambda: tk_b200.gemm_raw(256, 256, 256, a, 256, b, 256, c, 256), iters, flush)
+    # Back to back, as the reference's attention benchmark counts public calls.
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(512):
+        tk_b200.gemm_raw(256, 256, 256, a, 256, b, 256, c, 256)
+    t1.record()
+    torch.cuda.synchronize()
+    out["gemm_256"] = tensor_entry(med, gemm_flops(256, 256, 256),
+                                   {"us_per_call": round(med * 1e3, 2), "us_per_call_back_to_back":
+                                    round(t0.elapsed_time(t1) / 512 * 1e3, 2), "timing": "L2 flushed between calls"})
+    del a, b, c
+
+    # cfg2: 1,048,576 tiles of 16 x 16 FP32, N(0, 4) (seed 1): each op alone and all four fused.
+    tiles = ROW_TILES
+    gen.manual_seed(1)
+    x = torch.randn(tiles * 256, device="cuda", generator=gen) * 2
+    rs = torch.empty(tiles * 16, device="cuda")
+    rm = torch.empty(tiles * 16, device="cuda")
+    sm = torch.empty(tiles * 256, device="cuda")
+    cs = torch.empty(tiles * 256, device="cuda")
+    rin = tiles * 1024
+    for name, kw, nbytes in [
+            ("row_sum", {"row_sum": rs}, rin + tiles * 64),
+            ("row_max", {"row_max": rm}, rin + tiles * 64),
+            ("row_softmax", {"softmax": sm}, rin + tiles * 1024),
+            ("row_softmax_causal", {"softmax_causal": cs}, rin + tiles * 1024),
+            ("row_ops_all4", {"row_sum": rs, "row_max": rm, "softmax": sm, "softmax_causal": cs},
+             rin + 2 * tiles * 64 + 2 * tiles * 1024)]:
+        med, best = time_calls(lambda kw=kw: tk_b200.row_ops_raw(x, tiles, **kw), iters)
+        extra = {"tiles": tiles}
+        tr = traffic.get("tile_row_ops_all4" if name == "row_ops_all4" else name, {})
+        if "dram_bytes_per_tile" in tr:
+            extra["traffic"] = round(tr["dram_bytes_per_tile"] * tiles)
+        out[f"rowops_{name}"] = hbm_entry(med, nbytes, extra)
+    del x, rs, rm, sm, cs
+
+    # cfg3 fused variants: GEMM 8192^3 with the row-statistics epilogue, and with the
+    # full-row softmax (U[-1, 1], seed 2).
+    gen.manual_seed(2)
+    a = (torch.rand(GEMM_M, GEMM_K, device="cuda", generator=gen) * 2 - 1).half()
+    b = (torch.rand(GEMM_K, GEMM_N, device="cuda", generator=gen) * 2 - 1).half()
+    c = torch.empty(GEMM_M, GEMM_N, device="cuda")
+    mx = torch.empty(GEMM_M, device="cuda")
+    sm_ = torch.empty(GEMM_M, device="cuda")
+    med, _ = time_calls(lambda: tk_b200.gemm_raw(GEMM_M, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, c, GEMM_N), iters)
+    out["gemm_8192"] = tensor_entry(med, gemm_flops())
+    med, _ = time_calls(lambda: tk_b200.gemm_rowstats_raw(GEMM_M, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, c, GEMM_N,
+                                                          mx, sm_), iters)
+    out["gemm_8192_rowstats"] = tensor_entry(med, gemm_flops(), {"outputs": "C + row_max + row_sum"})
+    med, _ = time_calls(lambda: tk_b200.gemm_rowsoftmax_raw(GEMM_M, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, c, GEMM_N,
+                                                            c, GEMM_N), iters)
+    out["gemm_8192_rowsoftmax"] = tensor_entry(med, gemm_flops(), {"outputs": "P (softmax of C, in place)"})
+    del a, b, c, mx, sm_
+
+    # cfg4a: M = 16384, N = 4096, K = 14336, lda = K + 64, ldb = ldc = N + 32, N(0, 0.02^2) (seed 3).
+    m4, n4, k4 = 16384, 4096, 14336
+    lda, ldb, ldc = k4 + 64, n4 + 32, n4 + 32
+    gen.manual_seed(3)
+    a = (torch.randn(m4, lda, device="cuda", generator=gen) * 0.02).half()
+    b = (torch.randn(k4, ldb, device="cuda", generator=gen) * 0.02).half()
+    c = torch.empty(m4, ldc, device="cuda")
+    med, _ = time_calls(lambda: tk_b200.gemm_raw(m4, n4, k4, a, lda, b, ldb, c, ldc), iters)
+    out["gemm_16384x4096x14336_padded"] = tensor_entry(med, gemm_flops(m4, n4, k4),
+                                                      {"lda": lda, "ldb": ldb, "ldc": ldc})
+    del a, b, c
+
+    # cfg4b: decode-shaped M = 16, N = K = 4096 (seed 3): HBM-bound (B is 32 MiB).
+    gen.manual_seed(3)
+    a = (torch.randn(16, 4096, device="cuda", generator=gen) * 0.02).half()
+    b = (torch.randn(4096, 4096, device="cuda", generator=gen) * 0.02).half()
+    c = torch.empty(16, 4096, device="cuda")
+    med, _ = time_calls(lambda: tk_b200.gemm_raw(16, 4096, 4096, a, 4096, b, 4096, c, 4096), iters, flush)
+    nbytes = 16 * 4096 * 2 + 4096 * 4096 * 2 + 16 * 4096 * 4
+    out["gemm_16x4096x4096_decode"] = hbm_entry(med, nbytes, {"TFLOP/s": round(gemm_flops(16, 4096, 4096) / med / 1e9, 2),
+                                                              "timing": "L2 flushed between calls",
+                                                              "us_per_call": round(med * 1e3, 2)})
+    del a, b, c
+
+    # cfg5a: the one-tile attention (16 x 16, scale 1/4, N(0, 1), seed 4), unmasked and causal.
+    gen.manual_seed(4)
+    q = torch.randn(16, 16, device="cuda", generator=gen).half()
+    k = torch.randn(16, 16, device="cuda", generator=gen).half()
+    v = torch.randn(16, 16, device="cuda", generator=gen).half()
+    o = torch.empty(16, 16, device="cuda")
+    for causal in (False, True):
+        med, _ = time_calls(lambda causal=causal: tk_b200.attention_16x16_raw(q, k, v, o, causal), iters, flush)
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(2048):
+            tk_b200.attention_16x16_raw(q, k, v, o, causal)
+        t1.record()
+        torch.cuda.synchronize()
+        out["attention_16x16" + ("_causal" if causal else "")] = {
+            "bound": "latency", "us_per_call": round(med * 1e3, 2),
+            "us_per_call_back_to_back": round(t0.elapsed_time(t1) / 2048 * 1e3, 2),
+            "timing": "device time per call with L2 flushed between calls; back to back: 2048 public calls"}
+    del flush
+    return out
+
+
+def host_link(rank, world, h2d_tensors, d2h_tensors, reps=3):
+    """Pinned host <-> device copy bandwidth with every rank copying at once: the step's
+    inputs in and its outputs out, the two directions on separate streams. Returns the
+    per-rank and aggregate GB/s (max over ranks of the time)."""
+    import torch
+    hin = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in h2d_tensors]
+    hout = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in d2h_tensors]
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    nbytes = sum(t.numel() * t.element_size() for t in h2d_tensors + d2h_tensors)
+    best = None
+    for _ in range(reps):
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        s_in.wait_event(e0)
+        s_out.wait_event(e0)
+        with torch.cuda.stream(s_in):
+            for h, d in zip(hin, h2d_tensors):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for h, d in zip(hout, d2h_tensors):
+                h.copy_(d, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(s_in)
+        torch.cuda.current_stream().wait_stream(s_out)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1), world)
+        best = ms if best is None else min(best, ms)
+    del hin, hout
+    per_rank = nbytes / (best / 1e3) / 1e9
+    return {"bytes_per_rank": nbytes, "ms": round(best, 3), "GB/s_per_rank": round(per_rank, 1),
+            "GB/s_aggregate": round(per_rank * world, 1), "ranks_copying": world}
+
+
+def run_multi_gpu(rank, world, peaks, iters=10):
+    """Fixed-size problems split across the ranks (strong scaling) and gathered outputs.
+    Every rank takes the same collective steps in the same order. Times are per call,
+    between CUDA events after a barrier, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    import tk_b200
+    from tk_b200 import dist as tkd
+    gen = torch.Generator(device="cuda")
+    burst = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    out = {}
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ts.sort()
+        return max_over_ranks(ts[len(ts) // 2], world)
+
+    def check(code):
+        if code != 0:
+            raise RuntimeError(f"call failed with cudaError {code}")
+
+    # GEMM 8192^3 split by M: rank r computes rows [r0, r1) of C; B replicated.
+    r0, r1 = tkd.gemm_rows(GEMM_M, world, rank)
+    rows = r1 - r0
+    gen.manual_seed(2)
+    a_full = (torch.rand(GEMM_M, GEMM_K, device="cuda", generator=gen) * 2 - 1).half()
+    b = (torch.rand(GEMM_K, GEMM_N, device="cuda", generator=gen) * 2 - 1).half()
+    a = a_full[r0:r1].contiguous()
+    del a_full
+    c = torch.empty(rows, GEMM_N, device="cuda")
+    ms = timed(lambda: check(tk_b200.gemm_raw(rows, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, c, GEMM_N)))
+    tf = gemm_flops() / (ms / 1e3) / 1e12
+    out["gemm_8192_strong"] = {"ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_per_gpu": round(tf / world / burst, 4),
+                               "rows_per_rank": rows}
+    # ... with C gathered on every rank: fused into the GEMM epilogue (stores into every
+    # rank's IPC-mapped buffer over NVLink), or the GEMM then an NCCL all-gather.
+    gbuf = tkd.GatheredBuffer(GEMM_M, GEMM_N)
+    ms = timed(lambda: check(tk_b200.gemm_gather_raw(rows, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, gbuf.ptrs, rank,
+                                                     GEMM_N)))
+    link = (world - 1) * rows * GEMM_N * 4
+    out["gemm_8192_strong_gather_fused"] = {"ms": round(ms, 4), "TFLOP/s": round(gemm_flops() / (ms / 1e3) / 1e12, 1),
+                                            "nvlink_bytes_out_per_rank": link,
+                                            "nvlink_GB/s_out_per_rank": round(link / (ms / 1e3) / 1e9, 1)}
+    gbuf.close()
+    full = torch.empty(GEMM_M, GEMM_N, device="cuda")
+
+    def gemm_then_nccl():
+        check(tk_b200.gemm_raw(rows, GEMM_N, GEMM_K, a, GEMM_K, b, GEMM_N, c, GEMM_N))
+        dist.all_gather_into_tensor(full, c)
+    ms = timed(gemm_then_nccl)
+    out["gemm_8192_strong_gather_nccl"] = {"ms": round(ms, 4), "TFLOP/s": round(gemm_flops() / (ms / 1e3) / 1e12, 1)}
+    del a, b, c, full
+
+    # Attention [8, 32, 4096, 128] split by batch x head (unmasked and causal), and the
+    # unmasked output gathered with NCCL.
+    s0, s1 = tkd.attention_slices(ATT_B, ATT_H, world, rank)
+    nbh = s1 - s0
+    gen.manual_seed(4)
+    q = torch.randn(nbh, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    k = torch.randn(nbh, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    v = torch.randn(nbh, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    o = torch.empty(nbh, ATT_S, ATT_D, device="cuda")
+    scale = 1.0 / math.sqrt(ATT_D)
+    for causal in (False, True):
+        ms = timed(lambda causal=causal: check(tk_b200.attention_raw(q, k, v, o, 1, nbh, ATT_S, ATT_D, scale, causal)))
+        tf = attn_flops(causal) / (ms / 1e3) / 1e12
+        out["attention_fwd_strong" + ("_causal" if causal else "")] = {
+            "ms": round(ms, 4), "TFLOP/s": round(tf, 1), "frac_per_gpu": round(tf / world / burst, 4),
+            "heads_per_rank": nbh}
+    o_full = torch.empty(ATT_B * ATT_H, ATT_S, ATT_D, device="cuda")
+
+    def attn_then_nccl():
+        check(tk_b200.attention_raw(q, k, v, o, 1, nbh, ATT_S, ATT_D, scale, False))
+        dist.all_gather_into_tensor(o_full, o)
+    ms = timed(attn_then_nccl)
+    out["attention_fwd_strong_gather_nccl"] = {"ms": round(ms, 4),
+                                               "TFLOP/s": round(attn_flops(False) / (ms / 1e3) / 1e12, 1)}
+    del q, k, v, o, o_full
+
+    # Row ops, 1,048,576 tiles split by tile range, all four ops fused.
+    t0_, t1_ = tkd.tile_range(ROW_TILES, world, rank)
+    nt = t1_ - t0_
+    gen.manual_seed(1)
+    x = torch.randn(nt * 256, device="cuda", generator=gen) * 2
+    rs = torch.empty(nt * 16, device="cuda")
+    rm = torch.empty(nt * 16, device="cuda")
+    sm = torch.empty(nt * 256, device="cuda")
+    cs = torch.empty(nt * 256, device="cuda")
+    ms = timed(lambda: check(tk_b200.row_ops_raw(x, nt, rs, rm, sm, cs)))
+    nbytes = ROW_TILES * (1024 + 2 * 64 + 2 * 1024)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    out["rowops_all4_strong"] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_per_gpu": round(gbs / world / hbm, 4),
+                                 "tiles_per_rank": nt}
+    del x, rs, rm, sm, cs
+    return out
+
+
+def workload_config(args, world):
+    """The `config` object of both arms' JSON lines."""
+    return {
+        "workload": {"headline": "GEMM f16 8192x8192x8192 -> f32 + attention fwd [8,32,4096,128] "
+                                 "unmasked + causal, per GPU",
+                     "gemm": "GEMM f16 8192x8192x8192 -> f32, per GPU",
+                     "attention": "attention fwd [8,32,4096,128] unmasked + causal, per GPU",
+                     "rowops": f"{args.row_tiles:,} 16x16 FP32 tiles, sum+max+softmax+causal in one pass, "
+                               "per GPU"}[args.workload],
+        "parallelism": f"dp{world} (GEMM by M row blocks, attention by batch x head, row ops by tile range)",
+        "l2": "inputs larger than L2 (126 MB): no flush needed",
+        "gather": args.gather or False,
+    }
 
 
 def main_ours(args):
@@ -451,20 +827,33 @@ def main_ours(args):
                                                                                         local)
     peaks, peak_src = load_peaks()
     traffic = load_traffic()
+    timed_seconds = ms_per_step * args.steps / 1e3
     if args.workload == "rowops":
         unit, metric_scale, peak_key = "GB/s", 1e9, "hbm_gbs"
         metric = "tile row ops (sum, max, softmax, causal softmax) HBM GB/s"
         dtype = "f32"
     else:
-        unit, metric_scale, peak_key = "TFLOP/s", 1e12, "bf16_tflops_sustained"
+        unit, metric_scale = "TFLOP/s", 1e12
+        _, peak_key = tensor_peak(peaks, timed_seconds)
         metric = ("FP16 GEMM TFLOP/s @8192^3 + attn-fwd TFLOP/s, % of B200 peak, at 1/2/4/8 GPUs")
         dtype = "f16 in, f32 accumulate/out"
+    # The hosts' copy ceiling for e2e: the step's bytes in and out, every rank at once.
+    link = host_link(rank, world, wl.h2d, wl.d2h)
+    link["e2e_ceiling"] = round(work_per_step / (link["ms"] / 1e3) / metric_scale, 2)
+    link["e2e_ceiling_unit"] = unit
+    configs = None
+    multi = None
+    if not args.no_configs and args.workload == "headline":
+        if world == 1:
+            configs = run_configs(peaks, traffic)
+        else:
+            multi = run_multi_gpu(rank, world, peaks)
     value = work_per_step / (ms_per_step / 1e3) / metric_scale
     e2e_value = work_per_step / (e2e_ms / 1e3) / metric_scale
 
     # Roofline of the dominant kernel (largest share of step time).
-    dom = max(range(len(wl.calls)), key=lambda i: per_kernel_ms[i])
-    name, _, work, _ = wl.calls[dom]
+    dom = max(range(len(wl.call_meta)), key=lambda i: per_kernel_ms[i])
+    name, work = wl.call_meta[dom]
     achieved = work / (per_kernel_ms[dom] / 1e3) / metric_scale
     peak = peaks.get(peak_key, FALLBACK_PEAKS[peak_key])
     entry = traffic.get(name, {}) if traffic else {}
@@ -474,11 +863,12 @@ def main_ours(args):
         traffic_bytes = round(entry["dram_bytes_per_tile"] * args.row_tiles)
     roofline = {"kernel": name, "bound": "hbm" if unit == "GB/s" else "tensor", "achieved": round(achieved, 1),
                 "peak": peak, "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic_bytes,
-                "peak_source": f"{peak_src} {peak_key}"}
+                "peak_source": f"{peak_src} {peak_key} (timed region {timed_seconds:.2f} s)"}
     if unit == "TFLOP/s":
-        roofline["frac_of_burst"] = round(achieved / peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]), 4)
+        roofline["frac_of_sustained"] = round(
+            achieved / peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]), 4)
     components = {}
-    for (cname, _, cwork, _), ms in zip(wl.calls, per_kernel_ms):
+    for (cname, cwork), ms in zip(wl.call_meta, per_kernel_ms):
         rate = cwork / (ms / 1e3) / metric_scale
         components[cname] = {"ms": round(ms, 4), unit: round(rate, 1), "frac": round(rate / peak, 4)}
 
@@ -489,20 +879,11 @@ def main_ours(args):
             threads = min(os.cpu_count() or 1, 64)
             res = cpu_baseline(threads, args.workload)
             if res is not None:
-                tflops, kind, sample, secs = res
-                cpu = {"value": tflops, "unit": unit, "cores": threads, "kind": kind,
-                       "sample": f"{sample}; {secs:.1f} s of CPU time, scaled to the step's FLOP mix"}
-        config = {
-            "workload": {"headline": "GEMM f16 8192x8192x8192 -> f32 + attention fwd [8,32,4096,128] "
-                                     "unmasked + causal, per GPU",
-                         "gemm": "GEMM f16 8192x8192x8192 -> f32, per GPU",
-                         "attention": "attention fwd [8,32,4096,128] unmasked + causal, per GPU",
-                         "rowops": f"{args.row_tiles:,} 16x16 FP32 tiles, sum+max+softmax+causal in one pass, "
-                                   "per GPU"}[args.workload],
-            "parallelism": f"dp{world} (GEMM by M row blocks, attention by batch x head, row ops by tile range)",
-            "l2": "inputs larger than L2 (126 MB): no flush needed",
-            "gather": args.gather or False,
-        }
+                tflops, kind, sample, secs, legs = res
+                cpu = {"value": tflops, "unit": unit, "cores": threads, "kind": kind, "legs": legs,
+                       "sample": f"{sample}; {secs:.1f} s wall with {threads} threads, scaled to the step's "
+                                 "FLOP mix"}
+        config = workload_config(args, world)
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -510,9 +891,13 @@ def main_ours(args):
             "config": config, "roofline": roofline, "components": components,
             "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d * world,
                     "d2h_bytes_per_step": d2h * world},
-            "gpu_launches": sum(c[3] for c in wl.calls) * args.steps,
-            "clocks": clocks, "cpu_baseline": cpu,
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clocks, "cpu_baseline": cpu, "host_link": link,
         }
+        if configs is not None:
+            line["configs"] = configs
+        if multi is not None:
+            line["multi_gpu"] = multi
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -537,7 +922,7 @@ def main_reference(args):
     else:
         unit = "TFLOP/s"
         metric = "FP16 GEMM TFLOP/s @8192^3 + attn-fwd TFLOP/s, % of B200 peak, at 1/2/4/8 GPUs"
-    values, kinds, samples, secs = [], set(), "", []
+    values, kinds, samples, secs, legs = [], set(), "", [], {}
     for i in range(args.warmup + args.steps):
         if args.workload == "rowops":
             import numpy as np
@@ -562,9 +947,10 @@ def main_reference(args):
             dt = time.perf_counter() - t0
             val = (n * 1024 * 3 + n * 128) / dt / 1e9
             kind, sample = "port", f"{n} tiles (restated row-tree and FP64 softmax oracles)"
+            legs = {"rowops": "port"}
         else:
-            # About 1.5 s of CPU work per step, so the whole run stays within minutes.
-            val, kind, sample, dt = cpu_baseline(threads, args.workload, gemm_rows=4, attn_rows=128)
+            # The cpu_baseline leg's sample: about 1.5 s per step with all host threads.
+            val, kind, sample, dt, legs = cpu_baseline(threads, args.workload)
         if i >= args.warmup:
             values.append(val)
             kinds.add(kind)
@@ -577,8 +963,9 @@ def main_reference(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(secs) * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (host oracle)",
         "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "sample_per_step": samples},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind, "sample": samples},
+        "config": dict(workload_config(args, world), sample_per_step=samples),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": kind, "legs": legs,
+                         "sample": samples},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -599,6 +986,8 @@ def main():
                     help="tiles per GPU of the rowops workload (default 1,048,576; inputs stay larger than L2 "
                          "above 126,000)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the per-configuration (N = 1) and multi-GPU (N > 1) measurements")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -226,11 +226,12 @@ TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, co
                                                 cudaStream_t stream);
 
 /* No counterpart in the reference (a tuning switch). Attention with head_dim 128,
- * more than 128 keys and a positive scale runs on CTA pairs (tcgen05 cta_group::2,
- * M = 256 tiles) by default; 1 selects the single-CTA kernel for those problems
- * instead, 0 or 2 the CTA-pair kernel. Both give results inside the same bound.
- * Returns the previous setting (0 or 1); other values only query it. Process-wide;
- * every call reads it. */
+ * more than 128 keys and a positive scale has two kernels: 1 (also 0, the
+ * default) selects the single-CTA persistent kernel, 2 the CTA-pair kernel
+ * (tcgen05 cta_group::2, M = 256 tiles, every MMA with both operands K-major in
+ * shared memory). Both give results inside the same bound; the single-CTA kernel
+ * is the faster on B200. Returns the previous setting (1 or 2); other values only
+ * query it. Process-wide; every call reads it. */
 TK_API int tk_attention_set_cta_group(int cta_group);
 
 /* ---- status ------------------------------------------------------------------ */

@@ -21,6 +21,18 @@ pytestmark = pytest.mark.gpu
 GUARD_BEFORE, GUARD_AFTER = -12345.0, 12345.0  # tests/attention_correctness.cu:22-23
 
 
+@pytest.fixture(params=[1, 2], ids=["cta1", "cta_pair"])
+def attn_kernel(request):
+    """head_dim 128 multi-block problems have two kernels: the single-CTA one (1, the
+    default) and the CTA-pair one (2, tcgen05 cta_group::2). Both run every case."""
+    lib = tk_b200.lib()
+    old = lib.tk_attention_set_cta_group(request.param)
+    try:
+        yield request.param
+    finally:
+        lib.tk_attention_set_cta_group(old)
+
+
 def run_tile(q, k, v, causal, stream=None, alias=False):
     qkv = dev(np.concatenate([q.reshape(-1), k.reshape(-1), v.reshape(-1)]))
     buf = torch.full((258,), float("nan"), device="cuda")
@@ -117,13 +129,13 @@ def test_general_shapes(shape, causal):
     general_case(b, h, s, d, causal, seed=sum(shape))
 
 
-def test_general_aliased_and_misaligned():
+def test_general_aliased_and_misaligned(attn_kernel):
     general_case(1, 2, 200, 64, True, seed=5, alias=True)
     general_case(1, 1, 200, 128, False, seed=6, misaligned=True)
 
 
 @pytest.mark.parametrize("causal", [False, True])
-def test_large_8x32x4096x128_sampled(causal):
+def test_large_8x32x4096x128_sampled(causal, attn_kernel):
     """The large configuration (seed 4, N(0, 1), scale 1/sqrt(128)); 4 (b, h) pairs x
     sampled query rows including the first and last."""
     rng = np.random.default_rng(1)
@@ -166,14 +178,14 @@ def test_more_items_than_sms_every_head(causal):
 @pytest.mark.parametrize("shape", [(1, 1, 1, 128), (2, 3, 128, 128), (1, 2, 129, 128), (1, 1, 300, 128),
                                    (2, 1, 1000, 128), (1, 2, 517, 128)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("causal", [False, True])
-def test_head128_shapes(shape, causal):
+def test_head128_shapes(shape, causal, attn_kernel):
     """head_dim 128 on single-block, tail and multi-block shapes."""
     b, h, s, d = shape
     general_case(b, h, s, d, causal, seed=11 + sum(shape))
 
 
 @pytest.mark.parametrize("causal", [False, True])
-def test_head128_many_items_gqa_and_misaligned(causal):
+def test_head128_many_items_gqa_and_misaligned(causal, attn_kernel):
     """More items than SMs (dynamic scheduling), grouped-query heads and misaligned
     operands at head_dim 128."""
     general_case(1, 160, 512, 128, causal, seed=21)
@@ -196,7 +208,7 @@ def test_head128_many_items_gqa_and_misaligned(causal):
 
 
 @pytest.mark.parametrize("scale", [-0.3, 0.0])
-def test_non_positive_scale(scale):
+def test_non_positive_scale(scale, attn_kernel):
     """A negative or zero scale (scores are scaled before the max; masked keys stay -inf)."""
     b, h, s, d = 1, 2, 300, 128
     q, k, v = oracle.gen_qkv_normal(31, 1.0, b * h * s * d)
@@ -210,3 +222,28 @@ def test_non_positive_scale(scale):
             want = oracle.attention_ref(q[sl], k[sl], v[sl], s, d, scale, causal)
             bound = oracle.attention_bound(v[sl], s, d)
             assert np.all(np.abs(got[bh] - want) <= bound[None, :]), (causal, bh)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_cta_pair_kernel_matches_single_cta(causal):
+    """The two head_dim 128 kernels on the same inputs: both inside the bound (checked
+    above); here they also agree with each other to within the same bound, over every
+    row of a multi-item problem with a ragged tail (S = 1300)."""
+    b, h, s, d = 1, 6, 1300, 128
+    q, k, v = oracle.gen_qkv_normal(77, 1.0, b * h * s * d)
+    tq, tk_, tv = dev(q), dev(k), dev(v)
+    lib = tk_b200.lib()
+    outs = []
+    old = lib.tk_attention_set_cta_group(1)
+    try:
+        for kernel in (1, 2):
+            lib.tk_attention_set_cta_group(kernel)
+            out = torch.full((b * h * s * d,), float("nan"), device="cuda")
+            assert tk_b200.attention_raw(tq, tk_, tv, out, b, h, s, d, 1 / math.sqrt(d), causal) == 0
+            outs.append(host(out).reshape(b * h, s, d))
+    finally:
+        lib.tk_attention_set_cta_group(old)
+    for bh in range(b * h):
+        bound = oracle.attention_bound(v.reshape(b * h, s, d)[bh], s, d)
+        assert np.all(np.abs(outs[0][bh] - outs[1][bh]) <= 2 * bound[None, :]), bh
+    assert tk_b200.device_status() == 0

@@ -56,9 +56,15 @@ constexpr int kQOff = 0;
 constexpr int kPOff = 2 * kTileBytes;
 constexpr int kKvOff = 4 * kTileBytes;
 constexpr int kBarOff = kKvOff + kSlots * kSlotBytes;
-constexpr int kSmemBytes = kBarOff + 256 + 1024;  // + barriers, + alignment slack
+constexpr int kSmemBytes = kBarOff + 256 + 1024;  // + barriers (21 x 8 B, TMEM slot, abort flag), + alignment slack
 constexpr int kRowsPerItem = 512;                 // two 256-row tiles of the pair
 constexpr uint32_t kIdesc = idesc_f16_f32(256, 128, 0, 0);
+// The two softmax warps of an SM sub-partition (one per tile) take turns on the MUFU
+// unit for the exponentials of blocks both tiles process.
+#ifndef TK_ATTN_PAIR_MUFU_TURNS
+#define TK_ATTN_PAIR_MUFU_TURNS 1
+#endif
+constexpr bool kMufuTurns = TK_ATTN_PAIR_MUFU_TURNS != 0;
 static_assert(kSmemBytes <= 232448, "shared memory above the sm_100 per-block limit");
 
 struct PairParams {
@@ -121,7 +127,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto p_ready = [&](int g) { return bars + 8u * (2 * kSlots + 6 + g); };
     auto pv_done = [&](int g) { return bars + 8u * (2 * kSlots + 8 + g); };
     auto o_empty = [&](int g) { return bars + 8u * (2 * kSlots + 10 + g); };
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 8 * (2 * kSlots + 12));
+    // MUFU turn of the two softmax warps that share an SM sub-partition (warp q of tile 0
+    // and warp q + 4 of tile 1): turn(g, q) completes when tile g's warp q may run the
+    // exponentials of its next block shared with the other tile.
+    auto turn = [&](int g, uint32_t q) { return bars + 8u * (2 * kSlots + 12 + 4 * g + q); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kBarOff + 8 * (2 * kSlots + 20));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const uint32_t warp = warp_id();
@@ -144,6 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(p_ready(g), 8);
             mbar_init(pv_done(g), 1);
             mbar_init(o_empty(g), 8);
+            for (uint32_t q = 0; q < 4; ++q) mbar_init(turn(g, q), 1);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             // S_g may be overwritten once both CTAs' softmax warps hold S_g's last block in registers.
             auto s_writable = [&](int g) {
-                return s_issued[g] == 0 || mbar_wait_cluster(s_free(g), static_cast<uint32_t>(s_issued[g] - 1) & 1u,
+                return s_issued[g] == 0 || mbar_wait(s_free(g), static_cast<uint32_t>(s_issued[g] - 1) & 1u,
                                                              kFaultAttnWait, abort_flag);
             };
             for (int w = cluster_id; w < p.num_items && ok; w += num_clusters, ++items) {
@@ -273,6 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < it.nb_load && ok; ++j) {
                     ok = false;
                     // S of block j + 1 for both tiles: runs while the softmax of block j does.
+                    // Each tile's group is issued as soon as its own condition holds (waiting
+                    // for both tiles first measured slower: the pipe then idles on the later one).
                     if (j + 1 < it.nb_load) {
                         const int k_load = 2 * (j + 1);
                         if (!mbar_wait(kv_full(slot_of(k_load)), phase_of(k_load), kFaultAttnWait, abort_flag)) break;
@@ -296,13 +309,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bool pv_ok = true;
                     for (int g = 0; g < 2 && pv_ok; ++g) {
                         if (j >= it.nb[g]) continue;
-                        pv_ok = mbar_wait_cluster(p_ready(g), static_cast<uint32_t>(pv_issued[g]) & 1u, kFaultAttnWait,
-                                                  abort_flag);
+                        pv_ok = mbar_wait(p_ready(g), static_cast<uint32_t>(pv_issued[g]) & 1u, kFaultAttnWait,
+                                          abort_flag);
                         // The first PV of an item overwrites O_g: the previous item's O_g must
                         // have been read out of tensor memory by both CTAs.
                         if (pv_ok && j == 0 && outputs[g] > 0)
-                            pv_ok = mbar_wait_cluster(o_empty(g), static_cast<uint32_t>(outputs[g] - 1) & 1u,
-                                                      kFaultAttnWait, abort_flag);
+                            pv_ok = mbar_wait(o_empty(g), static_cast<uint32_t>(outputs[g] - 1) & 1u, kFaultAttnWait,
+                                              abort_flag);
                         if (pv_ok) {
                             tc_fence_after();
                             issue_pv(g, kv_addr(slot_of(v_load)), j == 0);
@@ -336,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float c = p.scale_log2;
         uint32_t s_seen = 0;  // S_g completions consumed
         uint32_t pv_count = 0;  // PV_g MMAs announced (one per processed block)
+        uint32_t turns = 0;     // blocks shared with the other tile processed so far
         bool ok = true;
         for (int w = cluster_id; w < p.num_items && ok; w += num_clusters) {
             const PairItem it = make_pair_item(w, p);
@@ -356,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // S_g is in registers: the next block's S may overwrite it.
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(s_free_lead);
+                if (lane == 0) mbar_arrive_remote(s_free_lead);
                 const int kv0 = 128 * j;
                 int limit = p.seq - kv0;
                 if (p.causal) limit = min(limit, q_row - kv0 + 1);
@@ -365,14 +379,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 next_point(m_run, row_max128(r) * c, m_use, alpha);
                 // PV_g,j-1 must have completed before O_g is rescaled or P_g overwritten
                 // (block 0's predecessor was waited for by the previous item's epilogue).
-                bool pv_prev_done = j == 0;
+                if (j > 0 && !mbar_wait_warp(pv_done(g), (pv_count - 1) & 1u, kFaultAttnWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
                 bool rescaled = false;
                 if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
-                    if (!mbar_wait_warp(pv_done(g), (pv_count - 1) & 1u, kFaultAttnWait, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    pv_prev_done = true;
                     tc_fence_after();
 #pragma unroll
                     for (int cc = 0; cc < 8; ++cc) {
@@ -385,42 +397,54 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     rescaled = true;
                 }
-                // Exponentials (packed FP32 arguments and sums), binary16 pairs.
+                // Blocks that both tiles process take turns on the MUFU unit: tile 0's
+                // exponentials of a shared block, then tile 1's, then tile 0's next, so the
+                // other warp's loads, maximum and stores overlap them instead of competing.
+                const bool shared_block = kMufuTurns && j < it.nb[0] && j < it.nb[1];
+                if (shared_block && !(g == 0 && turns == 0) &&
+                    !mbar_wait_warp(turn(g, quarter), static_cast<uint32_t>(g == 0 ? turns - 1 : turns) & 1u,
+                                    kFaultAttnWait, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                // Exponentials (packed FP32 arguments and sums) and binary16 P, stored chunk by
+                // chunk into the K-major 128-byte-swizzled tile: 16-byte chunk q of key box b at
+                // row * 128 + ((q ^ (row % 8)) * 16).
                 float2 acc[4];
 #pragma unroll
                 for (int t = 0; t < 4; ++t) acc[t] = make_float2(0.0f, 0.0f);
                 const float2 c2 = make_float2(c, c);
                 const float2 m2 = make_float2(-m_use, -m_use);
-                uint32_t pk[64];
 #pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float2 a = fma2(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), c2, m2);
-                    const float2 e = make_float2(ex2(a.x), ex2(a.y));
-                    acc[i & 3] = add2(acc[i & 3], e);
-                    pk[i] = pack_half2(e.x, e.y);
+                for (int ch = 0; ch < 16; ++ch) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int k2 = 8 * ch + 2 * i;
+                        const float2 a =
+                            fma2(make_float2(__uint_as_float(r[k2]), __uint_as_float(r[k2 + 1])), c2, m2);
+                        const float2 e = make_float2(ex2(a.x), ex2(a.y));
+                        acc[i] = add2(acc[i], e);
+                        pk[i] = pack_half2(e.x, e.y);
+                    }
+                    const uint32_t addr = p_row + static_cast<uint32_t>(ch >> 3) * 16384u +
+                                          ((static_cast<uint32_t>(ch & 7) ^ swz) << 4);
+                    st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
+                }
+                if (shared_block) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(turn(1 - g, quarter));
+                    ++turns;
                 }
                 const float2 s01 = add2(acc[0], acc[1]);
                 const float2 s23 = add2(acc[2], acc[3]);
                 const float2 st = add2(s01, s23);
                 const float e_sum = st.x + st.y;
-                if (!pv_prev_done &&
-                    !mbar_wait_warp(pv_done(g), (pv_count - 1) & 1u, kFaultAttnWait, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                // P row into the K-major 128-byte-swizzled tile: 16-byte chunk q of key box b
-                // at row * 128 + ((q ^ (row % 8)) * 16).
-#pragma unroll
-                for (int ch = 0; ch < 16; ++ch) {
-                    const uint32_t addr = p_row + static_cast<uint32_t>(ch >> 3) * 16384u +
-                                          ((static_cast<uint32_t>(ch & 7) ^ swz) << 4);
-                    st_shared_v4(addr, pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-                }
                 fence_proxy_async_smem();
                 if (rescaled) tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(p_ready_lead);
+                if (lane == 0) mbar_arrive_remote(p_ready_lead);
                 ++pv_count;
                 l_run = l_run * alpha + e_sum;
                 m_run = m_use;
@@ -444,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // O_g is in registers: the next item's first PV may overwrite it.
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive_cluster(o_empty_lead);
+                    if (lane == 0) mbar_arrive_remote(o_empty_lead);
                 }
                 if (row_ok) {
 #pragma unroll

@@ -649,9 +649,9 @@ int tk_gemm_set_cta_group(int cta_group) {
 }
 
 int tk_attention_set_cta_group(int cta_group) {
-    // 0 and 2: the CTA-pair kernel where it applies; 1: always the single-CTA kernel.
-    if (cta_group < 0 || cta_group > 2) return tk::attn::cta_group_knob().load() == 1 ? 1 : 0;
-    return tk::attn::cta_group_knob().exchange(cta_group == 1 ? 1 : 0) == 1 ? 1 : 0;
+    // 1 (or 0, the default): the single-CTA kernel; 2: the CTA-pair kernel where it applies.
+    if (cta_group < 0 || cta_group > 2) return tk::attn::cta_group_knob().load();
+    return tk::attn::cta_group_knob().exchange(cta_group == 2 ? 2 : 1);
 }
 
 int tk_gemm_set_splitk_reduce(int mode) {

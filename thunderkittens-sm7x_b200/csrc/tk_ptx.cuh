@@ -69,6 +69,14 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                  : "memory");
 }
 
+// Arrive on a barrier of a CTA of the cluster (address from mapa), default
+// (CTA-scope release) semantics: what must reach the barrier's owner is ordered by
+// the caller's own fences (tcgen05 fences, proxy fences). Measured on B200, the
+// cluster-scope release form costs about 1,000 cycles per arrival.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 // Arrive on a barrier in another CTA of the cluster (address from mapa).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
