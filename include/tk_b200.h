@@ -225,6 +225,13 @@ TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, co
                                                 int seq, int head_dim, float scale, int causal,
                                                 cudaStream_t stream);
 
+/* No counterpart in the reference (a tuning switch). Tile-rows per rasterisation
+ * group of the GEMM kernels' persistent tile walk: 0 (default) chooses by output shape
+ * (16, or 32 when the output has at most 16 tile-columns); 1..4096 forces a value. Results
+ * do not depend on it. Returns the previous setting; other values only query it.
+ * Process-wide; every call reads it. */
+TK_API int tk_gemm_set_group_rows(int rows);
+
 /* No counterpart in the reference (a tuning switch). Attention with head_dim 128,
  * more than 128 keys and a positive scale has two kernels: 1 (also 0, the
  * default) selects the single-CTA persistent kernel, 2 the CTA-pair kernel

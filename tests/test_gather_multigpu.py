@@ -1,7 +1,8 @@
 """The all-gather fused into the GEMM epilogue (tk_gemm_f16_f16_f32_nn_gather) on
-two GPUs, one process per GPU: every rank's gathered buffer holds every rank's row
-block within the GEMM error bound of the FP64 oracle, its padding untouched, and
-the ranks' copies are bit-identical. Skipped with fewer than two GPUs."""
+2, 4 and 8 GPUs, one process per GPU: every rank's gathered buffer holds every
+rank's row block within the GEMM error bound of the FP64 oracle, its padding
+untouched, and the ranks' copies are bit-identical. Each world size is skipped
+when the machine has fewer GPUs."""
 
 import os
 import socket
@@ -87,9 +88,10 @@ def _worker(rank, world, port, shapes, result_q):
     result_q.put((rank, errors))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_gemm_gather_fused_two_gpus():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gemm_gather_fused(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     shapes = [(512, 1024, 2048, 1024), (256, 784, 512, 790), (1024, 2048, 1024, 2048)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

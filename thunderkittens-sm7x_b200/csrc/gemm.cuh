@@ -20,8 +20,10 @@
 // 128 columns of B (no multicast), the even CTA issues the MMAs for both, and
 // each CTA's TMEM receives its 128 rows of the 256 x 256 accumulator.
 //
-// The persistent grid walks output tiles in groups of kGroupM tile-rows so that
-// the CTAs resident at one time share A row-blocks and B column-blocks in L2.
+// The persistent grid walks output tiles in groups of Params::group_m tile-rows,
+// column by column inside a group, so that the tiles resident at one time form a
+// compact block that shares A row-blocks and B column-blocks in L2. C is written
+// with evict-first stores so that the output stream does not displace A and B.
 //
 // Output shapes with too few tiles to fill the GPU split K: one work unit per
 // (tile, K split). The splits of a tile either form a thread-block cluster and sum
@@ -40,7 +42,7 @@ constexpr int kBlockM = 128;   // rows of C per CTA
 constexpr int kBlockN = 256;   // MMA N: columns of C per tile (128 in the small-M split-K variant)
 constexpr int kBlockK = 64;    // K per pipeline stage (one 128-byte swizzle row)
 constexpr int kMmaK = 16;      // K per tcgen05.mma (kind::f16)
-constexpr int kGroupM = 16;    // tile-rows per rasterisation group
+constexpr int kGroupM = 16;    // default tile-rows per rasterisation group
 constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 producer, 5 MMA
 constexpr int kMaxGatherRanks = 8;   // destinations of the all-gather epilogue
 
@@ -71,6 +73,7 @@ struct Params {
     long long ldc;
     bool c_vec4;        // c 16-byte aligned and ldc % 4 == 0
     int m_tiles, n_tiles, k_blocks;
+    int group_m;        // tile-rows per rasterisation group
     int num_tiles;      // m_tiles * n_tiles * k_splits work units
     // Split-K (small-M problems): unit t covers K blocks [ks * kb_per_split, ...)
     // and writes its partial C to ws[ks][m][n] (dense); splitk_reduce_kernel then
@@ -87,11 +90,11 @@ struct Params {
     long long dst_row0;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int* tm, int* tn) {
-    const int per_group = kGroupM * n_tiles;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int group_m, int* tm, int* tn) {
+    const int per_group = group_m * n_tiles;
     const int group = t / per_group;
-    const int first_m = group * kGroupM;
-    const int rows = min(kGroupM, m_tiles - first_m);
+    const int first_m = group * group_m;
+    const int rows = min(group_m, m_tiles - first_m);
     const int r = t - group * per_group;
     *tm = first_m + r % rows;
     *tn = r / rows;
@@ -100,7 +103,7 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // Output tile and K-block range of work unit t.
 __device__ __forceinline__ void work_coords(int t, const Params& p, int* tm, int* tn, int* kb0, int* kb1) {
     const int ks = t % p.k_splits;
-    tile_coords(t / p.k_splits, p.m_tiles, p.n_tiles, tm, tn);
+    tile_coords(t / p.k_splits, p.m_tiles, p.n_tiles, p.group_m, tm, tn);
     *kb0 = ks * p.kb_per_split;
     *kb1 = min(*kb0 + p.kb_per_split, p.k_blocks);
 }
@@ -384,13 +387,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 if (col0 + q * 4 < p.n) {
                                     float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-                                    *reinterpret_cast<float4*>(drow + col0 + q * 4) = v;
+                                    __stcs(reinterpret_cast<float4*>(drow + col0 + q * 4), v);
                                 }
                             }
                         } else {
 #pragma unroll
                             for (int q = 0; q < 32; ++q)
-                                if (col0 + q < p.n) drow[col0 + q] = __uint_as_float(r[q]);
+                                if (col0 + q < p.n) __stcs(drow + col0 + q, __uint_as_float(r[q]));
                         }
                     }
                 }

@@ -218,6 +218,22 @@ int split_cluster_capacity(int device, int splits) {
     return clusters;
 }
 
+// Tile-rows per rasterisation group. The tiles in flight at one time (one per CTA or
+// CTA pair: 148 or 74 on B200) walk a group column by column. Measured on B200
+// (CTA-pair tiles, TFLOP/s for 4 / 6 / 8 / 12 / 16 / 32 rows): 8192^3 1323 / 1360 /
+// 1389 / 1387 / 1423 / 1215; 16384 x 4096 x 14336 (16 tile-columns) 1216 / 1214 /
+// 1063 / 1070 / 1073 / 1202. DRAM reads at 8192^3 stay 4.5-5x the A + B bytes for 8
+// and 16 rows alike (1.22 / 1.36 GB), so the group size does not act through the
+// wave's L2 footprint alone. Hence: 16 rows, or 32 when the output has at most 16
+// tile-columns. Overridable for measurements.
+std::atomic<int> g_gemm_group_rows_override{0};
+
+int gemm_group_rows(int n_tiles) {
+    const int forced = g_gemm_group_rows_override.load(std::memory_order_relaxed);
+    if (forced > 0) return forced;
+    return n_tiles <= 16 ? 32 : tk::gemm::kGroupM;
+}
+
 // Tiling of a GEMM on single-CTA or CTA-pair tiles: tile width, K splits.
 struct GemmPlan {
     int bn = tk::gemm::kBlockN;  // columns per tile: 256, or 128 for small-M split-K
@@ -387,6 +403,7 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     }
     p.m_tiles = static_cast<int>(m_tiles);
     p.n_tiles = plan.n_tiles;
+    p.group_m = gemm_group_rows(p.n_tiles);
     p.k_blocks = k_blocks;
     p.k_splits = plan.k_splits;
     p.kb_per_split = plan.kb_per_split;
@@ -549,6 +566,7 @@ cudaError_t gemm_rowstats_noalloc(int m, int n, int k, const void* a, int lda, c
     const int tile_m = tk::gemm::kBlockM * cta_group;
     p.m_tiles = (m + tile_m - 1) / tile_m;
     p.n_tiles = static_cast<int>(n_tiles);
+    p.group_m = gemm_group_rows(p.n_tiles);
     p.k_blocks = (k + tk::gemm::kBlockK - 1) / tk::gemm::kBlockK;
     p.num_tiles = p.m_tiles * p.n_tiles;
     p.k_splits = 1;
@@ -652,6 +670,11 @@ int tk_attention_set_cta_group(int cta_group) {
     // 1 (or 0, the default): the single-CTA kernel; 2: the CTA-pair kernel where it applies.
     if (cta_group < 0 || cta_group > 2) return tk::attn::cta_group_knob().load();
     return tk::attn::cta_group_knob().exchange(cta_group == 2 ? 2 : 1);
+}
+
+int tk_gemm_set_group_rows(int rows) {
+    if (rows < 0 || rows > 4096) return g_gemm_group_rows_override.load();
+    return g_gemm_group_rows_override.exchange(rows);
 }
 
 int tk_gemm_set_splitk_reduce(int mode) {
