@@ -268,6 +268,8 @@ class Workload:
 
 def run_ours(args, rank, world, local):
     import torch
+    import tk_b200
+    tk_b200.lib().tk_attention_set_cta_group(2 if args.attention_kernel == "pair" else 1)
     fused = args.gather == "fused"
     wl = Workload(args.workload, rank, world, args.row_tiles, fused_gather=fused)
     wl.freeze()
@@ -845,6 +847,7 @@ def workload_config(args, world):
         "parallelism": f"dp{world} (GEMM by M row blocks, attention by batch x head, row ops by tile range)",
         "l2": "inputs larger than L2 (126 MB): no flush needed",
         "gather": args.gather or False,
+        "attention_kernel": args.attention_kernel,
     }
 
 
@@ -1015,6 +1018,8 @@ def main():
                     help="tiles per GPU of the rowops workload (default 1,048,576; inputs stay larger than L2 "
                          "above 126,000)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--attention-kernel", choices=["cta1", "pair"], default="cta1",
+                    help="head_dim 128 attention kernel: single-CTA (default) or CTA pair (tcgen05 cta_group::2)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-configuration (N = 1) and multi-GPU (N > 1) measurements")
     args = ap.parse_args()
