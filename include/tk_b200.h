@@ -225,6 +225,13 @@ TK_API cudaError_t tk_attention_forward_gqa_f16(const void* q, const void* k, co
                                                 int seq, int head_dim, float scale, int causal,
                                                 cudaStream_t stream);
 
+/* No counterpart in the reference (a tuning switch). GEMMs with m <= 64 (and no fused
+ * epilogue) run on an operand-swapped kernel by default (1): C^T = B^T A^T, so the rows
+ * of A become the tensor-core MMA's N dimension (16..64) and 128 columns of B its M;
+ * 0 selects the 128-row tiles instead. Both are inside the same error bound. Returns
+ * the previous setting; other values only query it. Process-wide. */
+TK_API int tk_gemm_set_small_m(int mode);
+
 /* No counterpart in the reference (a tuning switch). Tile-rows per rasterisation
  * group of the GEMM kernels' persistent tile walk: 0 (default) chooses by output shape
  * (16, or 32 when the output has at most 16 tile-columns); 1..4096 forces a value. Results

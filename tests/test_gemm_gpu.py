@@ -269,3 +269,38 @@ def test_gather_invalid_arguments():
     assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, [c.data_ptr(), 0], 0, 16) == bad  # null buffer
     assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p, 0, 8) == bad   # ldc < n
     assert tk_b200.gemm_gather_raw(16, 16, 16, a, 16, a, 16, p, 1, 16) == 0
+
+
+@pytest.mark.parametrize("m,n,k,lda,ldb,ldc", [
+    (16, 16, 16, 16, 16, 16), (16, 4096, 4096, 4096, 4096, 4096), (32, 784, 2048, 2056, 792, 787),
+    (48, 1040, 1024, 1024, 1040, 1044), (64, 20000, 96, 96, 20000, 20000), (64, 4096, 14336, 14400, 4128, 4128),
+    (16, 48, 8192, 8192, 48, 48)],
+    ids=["one_tile", "decode", "ragged_padded", "48_rows", "wide_short_k", "64_rows_long_k", "narrow_long_k"])
+def test_small_m_operand_swapped_kernel(m, n, k, lda, ldb, ldc):
+    """M <= 64 runs on the operand-swapped kernel (C^T = B^T A^T: the rows of A are the
+    MMA's N). Within the error bound, C padding untouched, bit-identical over two runs and
+    between the two split-K reduction forms (in the cluster / by the second kernel)."""
+    a, b = oracle.gen_gemm_normal(11, 0.02, m, n, k, lda, ldb)
+    sentinel = np.float32(-3.0)
+    prev = tk_b200.set_gemm_splitk_reduce(0)
+    try:
+        c0 = run_gemm(m, n, k, a, lda, b, ldb, ldc, sentinel=sentinel)
+        c0b = run_gemm(m, n, k, a, lda, b, ldb, ldc, sentinel=sentinel)
+        tk_b200.set_gemm_splitk_reduce(1)
+        c1 = run_gemm(m, n, k, a, lda, b, ldb, ldc, sentinel=sentinel)
+    finally:
+        tk_b200.set_gemm_splitk_reduce(prev)
+    assert np.array_equal(c0.view(np.uint32), c0b.view(np.uint32))
+    assert np.array_equal(c0.view(np.uint32), c1.view(np.uint32))
+    assert np.all(c0[:, n:] == sentinel)
+    check_rows(m, n, k, a, lda, b, ldb, c0, ldc, list(range(m)) if m * n <= 1 << 20 else sample_rows(m, 8))
+    assert tk_b200.device_status() == 0
+
+
+def test_small_m_misaligned_operands():
+    """Odd leading dimensions and misaligned bases (copied into dense buffers first) on the
+    operand-swapped kernel."""
+    m, n, k = 32, 1024, 512
+    a, b = oracle.gen_gemm_normal(12, 0.02, m, n, k, k + 3, n + 5)
+    c = run_gemm(m, n, k, a, k + 3, b, n + 5, n + 1)
+    check_rows(m, n, k, a, k + 3, b, n + 5, c, n + 1, list(range(m)))

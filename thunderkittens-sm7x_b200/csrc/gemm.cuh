@@ -509,6 +509,223 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small-M GEMM (M <= 64, decode-shaped): C^T = B^T A^T on the tensor core, so the
+// few rows of A become the MMA's N (16..64) and 128 columns of B its M. A tile of
+// 128 output columns then costs 4 MMAs of 128 x m_pad x 16 per 64-deep K block
+// (8x less tensor work than 128-row tiles of which M rows are used), and the kernel
+// streams B, the only large operand, at the rate of the loads in flight.
+//   MMA A = B tile (64 N x 64 K TMA boxes, MN-major: the same boxes as the GEMM's B)
+//   MMA B = A rows (64 K x m_pad rows, K-major)
+//   D (TMEM) = 128 lanes (output columns) x m_pad columns (output rows)
+// One CTA per (128-column tile, K split); small enough for two CTAs per SM. The K
+// splits of a tile form a cluster (CTA rank = split) and sum their partials in split
+// order over distributed shared memory (kCluster), or write them to scratch for
+// splitk_reduce_kernel (same order, same bits).
+// ---------------------------------------------------------------------------
+constexpr int kSkinnyStages = 4;
+constexpr int kSkinnyBN = 128;
+constexpr int kSkinnyMaxM = 64;
+constexpr int kSkinnyStageBytes = 2 * 8192 + kSkinnyMaxM * 128;  // B boxes + A box (up to 64 rows)
+constexpr int kSkinnySmemBytes = kSkinnyStages * kSkinnyStageBytes + 256 + 1024;
+
+struct SkinnyParams {
+    int m, n, k, m_pad;
+    float* c;
+    long long ldc;
+    bool c_vec4;
+    int n_tiles, k_blocks, k_splits, kb_per_split;
+    float* ws;  // split partials [k_splits][m][n] (second-kernel form), or null
+};
+
+template <bool kCluster>
+__global__ void __launch_bounds__(kThreads, 2)
+    skinny_kernel(const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_a,
+                  const SkinnyParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    const uint32_t base = (raw_base + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw_base);
+    const uint32_t bars = base + kSkinnyStages * kSkinnyStageBytes;
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (kSkinnyStages + s); };
+    const uint32_t tfull = bars + 8u * (2 * kSkinnyStages);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSkinnyStages * kSkinnyStageBytes + 8 * (2 * kSkinnyStages + 1));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_id();
+    const uint32_t lane = lane_id();
+    const int unit = static_cast<int>(blockIdx.x);
+    const int split = unit % p.k_splits;
+    const int tile = unit / p.k_splits;
+    const int n0 = tile * kSkinnyBN;
+    const int kb0 = split * p.kb_per_split;
+    const int kb1 = min(kb0 + p.kb_per_split, p.k_blocks);
+    const uint32_t tmem_cols = p.m_pad <= 32 ? 32u : 64u;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kSkinnyStages; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        mbar_init(tfull, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch_desc(&map_b);
+        tma_prefetch_desc(&map_a);
+    }
+    if (warp == 5) {
+        tmem_alloc<1>(smem_u32(tmem_slot), tmem_cols);
+        tmem_relinquish<1>();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    const uint32_t a_bytes = static_cast<uint32_t>(p.m_pad) * 128u;
+    if (warp == 4) {
+        // ---------------- producer ----------------
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = 0;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait_warp(empty_bar(stage), phase ^ 1u, kFaultProducerWait, abort_flag)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                const uint32_t dst = base + stage * kSkinnyStageBytes;
+                mbar_arrive_expect_tx(full_bar(stage), 2u * 8192u + a_bytes);
+                tma_load_2d(dst, &map_b, full_bar(stage), n0, kb * kBlockK);
+                tma_load_2d(dst + 8192, &map_b, full_bar(stage), n0 + 64, kb * kBlockK);
+                tma_load_2d(dst + 16384, &map_a, full_bar(stage), kb * kBlockK, 0);
+            }
+            __syncwarp();
+            ++issued;
+            if (++stage == kSkinnyStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (!ok) {
+            int s = stage;
+            uint32_t ph = phase;
+            for (int i = 0; i < min(issued, kSkinnyStages); ++i) {
+                if (--s < 0) {
+                    s = kSkinnyStages - 1;
+                    ph ^= 1u;
+                }
+                mbar_wait_warp(full_bar(s), ph, kFaultDrainWait, nullptr);
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        const uint32_t idesc = idesc_f16_f32(kSkinnyBN, p.m_pad, 1, 0);
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait_warp(full_bar(stage), phase, kFaultMmaWait, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t b_tile = base + stage * kSkinnyStageBytes;
+                const uint32_t a_rows = b_tile + 16384;
+#pragma unroll
+                for (int kk = 0; kk < kBlockK / kMmaK; ++kk)
+                    mma_f16_ss<1>(tmem, sw128_desc(b_tile + kk * 2048, 8192, 1024), sw128_desc(a_rows + kk * 32, 16, 1024),
+                                  idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                mma_commit(empty_bar(stage));
+            }
+            __syncwarp();
+            if (++stage == kSkinnyStages) {
+                stage = 0;
+                phase ^= 1u;
+            }
+        }
+        if (ok && lane == 0) mma_commit(tfull);
+        __syncwarp();
+    } else {
+        // ---------------- epilogue warps 0-3: lane = output column ----------------
+        const bool have = kb1 > kb0;
+        const bool ok = !have || mbar_wait_warp(tfull, 0u, kFaultEpilogueWait, abort_flag);
+        tc_fence_after();
+        const int col = n0 + static_cast<int>(warp * 32 + lane);
+        const bool col_ok = col < p.n;
+        float* part = reinterpret_cast<float*>(smem);  // [m_pad][128], over the consumed stages
+        for (int c = 0; c < p.m_pad / 16; ++c) {
+            uint32_t r[16];
+            if (have && ok) {
+                tmem_ld_32x32b_x16(tmem + ((warp * 32u) << 16) + 16u * c, r);
+                tmem_wait_ld();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) r[i] = 0u;  // an empty K range contributes zero
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int row = 16 * c + i;
+                const float v = __uint_as_float(r[i]);
+                if constexpr (kCluster) {
+                    part[row * kSkinnyBN + warp * 32 + lane] = v;
+                } else if (row < p.m && col_ok) {
+                    if (p.ws != nullptr)
+                        p.ws[(static_cast<long long>(split) * p.m + row) * p.n + col] = v;
+                    else
+                        __stcs(p.c + row * p.ldc + col, v);
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if constexpr (kCluster) {
+        // Every CTA of the cluster reaches both barriers, also after a timed-out wait
+        // (the fault is recorded and the call reports it).
+        cluster_sync();  // every split's partial is in its CTA's shared memory
+        const int quads = p.m * (kSkinnyBN / 4);
+        const int my = static_cast<int>(cluster_ctarank());
+        const int q_end = quads * (my + 1) / p.k_splits;
+        for (int q = quads * my / p.k_splits + static_cast<int>(threadIdx.x); q < q_end; q += kThreads) {
+            const int row = q / (kSkinnyBN / 4);
+            const int c4 = (q - row * (kSkinnyBN / 4)) * 4;
+            if (n0 + c4 >= p.n) continue;  // n is a multiple of 16: a quad is all in or all out
+            const uint32_t local = base + static_cast<uint32_t>((row * kSkinnyBN + c4) * 4);
+            // Split order, as splitk_reduce_kernel: bit-identical results.
+            float4 acc = ld_shared_cluster_f4(mapa_shared(local, 0));
+            for (int sp = 1; sp < p.k_splits; ++sp) {
+                const float4 v = ld_shared_cluster_f4(mapa_shared(local, static_cast<uint32_t>(sp)));
+                acc.x += v.x;
+                acc.y += v.y;
+                acc.z += v.z;
+                acc.w += v.w;
+            }
+            float* dst = p.c + static_cast<long long>(row) * p.ldc + n0 + c4;
+            if (p.c_vec4) {
+                __stcs(reinterpret_cast<float4*>(dst), acc);
+            } else {
+                dst[0] = acc.x;
+                dst[1] = acc.y;
+                dst[2] = acc.z;
+                dst[3] = acc.w;
+            }
+        }
+        cluster_sync();  // no CTA leaves while another still reads its shared memory
+    }
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc<1>(tmem, tmem_cols);
+    }
+}
+
 // Finishing pass of the fused row statistics: per row, combine the per-tile
 // partials in tile order with the same pairwise rule (binary-counter form: a
 // stack of complete power-of-two blocks, merged right to left at the end, which

@@ -155,8 +155,6 @@ cudaError_t launch_gemm_kernel(const CUtensorMap& ma, const CUtensorMap& mb, con
     return cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
 }
 
-std::atomic<int> g_gemm_splitk_mode{0};  // 0 = in-cluster reduction where it fits, 1 = always the separate kernel
-
 // Split-K with the reduction inside the kernel: grid = every work unit, clusters
 // of k_splits CTAs (one output tile each).
 template <int kBN>
@@ -280,6 +278,144 @@ GemmPlan plan_gemm(long long m_tiles, long long m, long long n, int k_blocks, bo
     return g;
 }
 
+// Small-M GEMM (M <= 64): sets skinny_kernel's shared-memory limit on `device`, once.
+cudaError_t skinny_configure(int device) {
+    static std::atomic<bool> configured[tk::host::kMaxDevices];
+    if (configured[device].load(std::memory_order_acquire)) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(tk::gemm::skinny_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         tk::gemm::kSkinnySmemBytes);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tk::gemm::skinny_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tk::gemm::kSkinnySmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[device].store(true, std::memory_order_release);
+    return cudaSuccess;
+}
+
+// How many clusters of `splits` CTAs of skinny_kernel can be resident at once on
+// `device` (cached; 0 when the query fails). skinny_configure must have succeeded.
+int skinny_cluster_capacity(int device, int splits) {
+    static std::atomic<int> cache[tk::host::kMaxDevices][9];
+    int v = cache[device][splits].load(std::memory_order_acquire);
+    if (v != 0) return v < 0 ? 0 : v;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(splits));
+    cfg.blockDim = dim3(tk::gemm::kThreads);
+    cfg.dynamicSmemBytes = tk::gemm::kSkinnySmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, tk::gemm::skinny_kernel<true>, &cfg) != cudaSuccess) {
+        static_cast<void>(cudaGetLastError());
+        clusters = 0;
+    }
+    cache[device][splits].store(clusters > 0 ? clusters : -1, std::memory_order_release);
+    return clusters;
+}
+
+std::atomic<int> g_gemm_splitk_mode{0};  // 0 = in-cluster reduction where it fits, 1 = always the separate kernel
+std::atomic<int> g_gemm_small_m{1};       // 1 = operand-swapped kernel for m <= 64, 0 = 128-row tiles
+
+// C = A B for m <= 64 on skinny_kernel: one CTA per (128-column tile, K split), two
+// CTAs per SM. Splits fill the GPU (at most 8, at least 2 K blocks each) and are
+// summed in split order: inside the tile's cluster when every cluster can be
+// resident at once (and the reduction mode allows it), else by splitk_reduce_kernel.
+cudaError_t skinny_gemm(int m, int n, int k, const void* a, long long lda, const void* b, long long ldb, float* c,
+                        long long ldc, bool c_vec4, int device, int sm_count, cudaStream_t stream) {
+    using namespace tk::gemm;
+    cudaError_t err = skinny_configure(device);
+    if (err != cudaSuccess) return err;
+    const int n_tiles = (n + kSkinnyBN - 1) / kSkinnyBN;
+    const int k_blocks = (k + kBlockK - 1) / kBlockK;
+    int splits = 1;
+    const int want = (2 * sm_count) / n_tiles;
+    if (want > 1 && k_blocks >= 4) splits = want < 8 ? want : 8;
+    if (splits > k_blocks / 2) splits = k_blocks / 2 > 1 ? k_blocks / 2 : 1;
+    int kb_per = (k_blocks + splits - 1) / splits;
+    splits = (k_blocks + kb_per - 1) / kb_per;
+    // The split count is lowered, if needed, to the largest whose tile clusters can all be
+    // resident at once; it does not depend on the reduction mode, so both forms give the
+    // same bits.
+    bool fits = false;
+    for (int s = splits; s >= 2 && !fits; --s) {
+        const int kp = (k_blocks + s - 1) / s;
+        const int ss = (k_blocks + kp - 1) / kp;
+        if (ss >= 2 && n_tiles <= skinny_cluster_capacity(device, ss)) {
+            splits = ss;
+            kb_per = kp;
+            fits = true;
+        }
+    }
+    const bool cluster = fits && g_gemm_splitk_mode.load(std::memory_order_relaxed) == 0;
+    SkinnyParams p{};
+    p.m = m;
+    p.n = n;
+    p.k = k;
+    p.m_pad = (m + 15) / 16 * 16;
+    p.c = c;
+    p.ldc = ldc;
+    p.c_vec4 = c_vec4;
+    p.n_tiles = n_tiles;
+    p.k_blocks = k_blocks;
+    p.k_splits = splits;
+    p.kb_per_split = kb_per;
+    p.ws = nullptr;
+    CUtensorMap mb, ma;
+    const uint64_t b_dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
+    const uint64_t b_strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t b_box[2] = {64, 64};
+    const uint64_t a_dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t a_strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t a_box[2] = {64, static_cast<uint32_t>(p.m_pad)};
+    if (!tk::host::make_map_f16(&mb, b, 2, b_dims, b_strides, b_box) ||
+        !tk::host::make_map_f16(&ma, a, 2, a_dims, a_strides, a_box)) {
+        return cudaErrorInvalidValue;
+    }
+    if (splits > 1 && !cluster) {
+        err = tk::host::scratch_alloc(reinterpret_cast<void**>(&p.ws),
+                                      static_cast<size_t>(splits) * m * n * sizeof(float), device, stream);
+        if (err != cudaSuccess) return err;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(n_tiles * splits));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSkinnySmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(splits);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cluster ? 1 : 0;
+    err = cluster ? cudaLaunchKernelEx(&cfg, skinny_kernel<true>, mb, ma, p)
+                  : cudaLaunchKernelEx(&cfg, skinny_kernel<false>, mb, ma, p);
+    if (p.ws != nullptr) {
+        if (err == cudaSuccess) {
+            const long long quads = static_cast<long long>(m) * (n / 4);
+            const int blocks = static_cast<int>(quads / 256 + 1 < 4 * sm_count ? quads / 256 + 1 : 4 * sm_count);
+            cudaLaunchConfig_t rcfg{};
+            rcfg.gridDim = dim3(static_cast<unsigned>(blocks));
+            rcfg.blockDim = dim3(256);
+            rcfg.stream = stream;
+            cudaLaunchAttribute rattr[1];
+            rattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            rattr[0].val.programmaticStreamSerializationAllowed = 1;
+            rcfg.attrs = rattr;
+            rcfg.numAttrs = 1;
+            err = cudaLaunchKernelEx(&rcfg, splitk_reduce_kernel, static_cast<const float*>(p.ws), splits, m, n, c, ldc,
+                                     c_vec4);
+        }
+        cudaFreeAsync(p.ws, stream);
+    }
+    return err;
+}
+
 // Destinations of the multi-GPU gathered GEMM: rank `rank` of `count` writes its m
 // rows at row rank * m of each buffer (count == 0: an ordinary GEMM into c).
 struct Gather {
@@ -350,6 +486,16 @@ cudaError_t gemm_impl(int m, int n, int k, const void* a, int lda, const void* b
     }
 
     int cta_group = g_gemm_cta_group_override.load(std::memory_order_relaxed);
+    // Up to 64 rows (decode-shaped): the operand-swapped kernel, unless CTA pairs are forced.
+    if (m <= tk::gemm::kSkinnyMaxM && !stats && !gathered && cta_group != 2 &&
+        g_gemm_small_m.load(std::memory_order_relaxed) != 0) {
+        err = skinny_gemm(m, n, k, a_use, lda_use, b_use, ldb_use, c, ldc, aligned(c, 16) && ldc % 4 == 0, device,
+                          sm_count, stream);
+        if (a_tmp) cudaFreeAsync(a_tmp, stream);
+        if (b_tmp) cudaFreeAsync(b_tmp, stream);
+        if (err != cudaSuccess) return err;
+        return cudaGetLastError();
+    }
     if (cta_group == 0) {
         const long long big_tiles = ((m + 255LL) / 256) * ((n + 255LL) / 256);
         cta_group = big_tiles >= sm_count / 2 ? 2 : 1;
@@ -675,6 +821,11 @@ int tk_attention_set_cta_group(int cta_group) {
 int tk_gemm_set_group_rows(int rows) {
     if (rows < 0 || rows > 4096) return g_gemm_group_rows_override.load();
     return g_gemm_group_rows_override.exchange(rows);
+}
+
+int tk_gemm_set_small_m(int mode) {
+    if (mode != 0 && mode != 1) return g_gemm_small_m.load();
+    return g_gemm_small_m.exchange(mode);
 }
 
 int tk_gemm_set_splitk_reduce(int mode) {

@@ -52,6 +52,7 @@ SIGNATURES = {
     "tk_attention_forward_gqa_f16": (_I, [_VP, _VP, _VP, _VP, _I, _I, _I, _I, _I, _F, _I, _VP]),
     "tk_attention_set_cta_group": (_I, [_I]),
     "tk_gemm_set_group_rows": (_I, [_I]),
+    "tk_gemm_set_small_m": (_I, [_I]),
     "tk_device_status": (_I, [C.POINTER(C.c_uint32), _I]),
     "tk_scratch_pool_bytes": (_I, [_I, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]),
     "tk_abi_version": (_I, []),
