@@ -670,7 +670,17 @@ def run_configs(peaks, traffic, iters=20):
     out["gemm_16x4096x4096_decode"] = hbm_entry(med, nbytes, {"TFLOP/s": round(gemm_flops(16, 4096, 4096) / med / 1e9, 2),
                                                               "timing": "L2 flushed between calls",
                                                               "us_per_call": round(med * 1e3, 2),
-                                                              "us_per_call_back_to_back_l2_resident": round(b2b, 2)})
+                                                              "us_per_call_back_to_back_l2_resident": round(b2b, 2),
+                                                              "kernel": "operand-swapped small-M kernel"})
+    # The same call on 128-row tiles (the path the operand-swapped kernel replaces), for comparison.
+    prev = tk_b200.lib().tk_gemm_set_small_m(0)
+    try:
+        med0, _ = time_calls(lambda: tk_b200.gemm_raw(16, 4096, 4096, a, 4096, b, 4096, c, 4096), iters, flush)
+    finally:
+        tk_b200.lib().tk_gemm_set_small_m(prev)
+    out["gemm_16x4096x4096_decode_row_tiles"] = hbm_entry(med0, nbytes, {"us_per_call": round(med0 * 1e3, 2),
+                                                                         "timing": "L2 flushed between calls",
+                                                                         "kernel": "128-row tiles, split-K"})
     del a, b, c
 
     # cfg5a: the one-tile attention (16 x 16, scale 1/4, N(0, 1), seed 4), unmasked and causal.

@@ -304,3 +304,20 @@ def test_small_m_misaligned_operands():
     a, b = oracle.gen_gemm_normal(12, 0.02, m, n, k, k + 3, n + 5)
     c = run_gemm(m, n, k, a, k + 3, b, n + 5, n + 1)
     check_rows(m, n, k, a, k + 3, b, n + 5, c, n + 1, list(range(m)))
+
+
+def test_small_m_kernel_and_row_tiles_agree():
+    """The decode shape 16 x 4096 x 4096 on both small-M paths (the operand-swapped kernel,
+    the default, and 128-row tiles): each within the error bound of the FP64 oracle."""
+    m, n, k = 16, 4096, 4096
+    a, b = oracle.gen_gemm_normal(3, 0.02, m, n, k, k, n)
+    r, s = oracle.gemm_ref(m, n, k, a, k, b, n)
+    prev = tk_b200.lib().tk_gemm_set_small_m(1)
+    try:
+        for mode in (1, 0):
+            tk_b200.lib().tk_gemm_set_small_m(mode)
+            c = run_gemm(m, n, k, a, k, b, n, n)
+            assert oracle.gemm_check(k, c, r, s, n, n)[0] == 0, mode
+    finally:
+        tk_b200.lib().tk_gemm_set_small_m(prev)
+    assert tk_b200.device_status() == 0
