@@ -30,7 +30,8 @@
 // Shared memory per CTA: Q_0, Q_1 (32 KiB each), P_0, P_1 (32 KiB each), a ring of
 // six 16 KiB slots that alternately hold this CTA's half of K_j and of V^T_j.
 //
-// MMA order of block j (even CTA, one thread): S_0,j+1, S_1,j+1, PV_0,j, PV_1,j.
+// MMAs (even CTA): one issuing thread per tile, each issuing S_g,j+1 then PV_g,j for
+// block j; the tensor pipe interleaves the two streams.
 // Softmax of tile g (four warps per CTA, one query row per thread): wait S_g,j;
 // load the row (tcgen05.ld); release S_g,j; mask, max, exponentials in registers;
 // rescale O_g only when the running max grows by more than 2^8 (after PV_g,j-1 has
@@ -48,7 +49,7 @@ namespace tk {
 namespace attn {
 namespace pair {
 
-constexpr int kThreads = 384;  // warps 0-7 softmax, 8 TMA, 9 TMEM + MMA, 10-11 idle
+constexpr int kThreads = 384;  // warps 0-7 softmax, 8 TMA, 9 TMEM + MMA (tile 0), 10 MMA (tile 1), 11 idle
 constexpr int kSlots = 6;
 constexpr int kTileBytes = 128 * 128 * 2;   // 128 rows x 128 binary16 (Q or P tile of one CTA)
 constexpr int kSlotBytes = 64 * 128 * 2;    // half a K block (64 keys x 128) or half a V^T block (64 x 128 keys)
@@ -144,10 +145,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(kv_full(s), 1);   // the even CTA's expect_tx; both CTAs' bytes
-            mbar_init(kv_empty(s), 1);  // MMA commit (multicast to both CTAs)
+            mbar_init(kv_empty(s), 2);  // one MMA commit (multicast to both CTAs) per issuer
         }
         mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
+        mbar_init(q_empty, 2);  // both issuers
         for (int g = 0; g < 2; ++g) {
             mbar_init(s_full(g), 1);
             mbar_init(s_free(g), 8);   // four softmax warps of each CTA
@@ -236,98 +237,103 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_wait(kv_full(s), ph, kFaultDrainWait, nullptr);
                 }
             }
-        } else if (warp == 9 && lane == 0 && leader) {
-            // ---------------- MMA issuer (even CTA, one thread) ----------------
+        } else if ((warp == 9 || warp == 10) && lane == 0 && leader) {
+            // ---------------- MMA issuers (even CTA): warp 9 tile 0, warp 10 tile 1 ----------------
+            // One issuing thread per tile: each waits only on its own tile's barriers, so
+            // while one waits (a wait costs the issuing thread 100-250 cycles even when the
+            // barrier has completed, and only a few MMAs queue behind an issue) the other
+            // keeps the tensor pipe fed. Both streams are shared-memory/K-major MMAs, so
+            // their interleaving costs nothing. K/V slots and Q are released by both
+            // issuers (barrier counts 2); a load that this tile does not read is released
+            // only after it has landed, which puts the release in the slot's current phase.
+            const int g = warp == 9 ? 0 : 1;
             auto kv_addr = [&](int s) { return base + kKvOff + static_cast<uint32_t>(s) * kSlotBytes; };
-            auto issue_s = [&](int g, uint32_t k_addr) {
+            auto issue_s = [&](uint32_t k_addr) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_f16_ss<2>(tmem + 128u * g, kmajor_desc(base + kQOff + g * kTileBytes, kk, 16384),
                                   kmajor_desc(k_addr, kk, 8192), kIdesc, kk > 0 ? 1u : 0u);
                 mma_commit_pair(s_full(g), 0x3);
             };
-            auto issue_pv = [&](int g, uint32_t vt_addr, bool first) {
+            auto issue_pv = [&](uint32_t vt_addr, bool first) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_f16_ss<2>(tmem + 256u + 128u * g, kmajor_desc(base + kPOff + g * kTileBytes, kk, 16384),
                                   kmajor_desc(vt_addr, kk, 8192), kIdesc, (!first || kk > 0) ? 1u : 0u);
                 mma_commit_pair(pv_done(g), 0x3);
             };
-            int s_issued[2] = {0, 0};
-            int pv_issued[2] = {0, 0};
-            int outputs[2] = {0, 0};
+            int s_issued = 0, pv_issued = 0, outputs = 0;
             int kv_base = 0, items = 0;
             bool ok = true;
-            // S_g may be overwritten once both CTAs' softmax warps hold S_g's last block in registers.
-            auto s_writable = [&](int g) {
-                return s_issued[g] == 0 || mbar_wait(s_free(g), static_cast<uint32_t>(s_issued[g] - 1) & 1u,
-                                                             kFaultAttnWait, abort_flag);
+            // S_g may be overwritten once both CTAs' softmax warps hold its last block in registers.
+            auto s_writable = [&]() {
+                return s_issued == 0 ||
+                       mbar_wait(s_free(g), static_cast<uint32_t>(s_issued - 1) & 1u, kFaultAttnWait, abort_flag);
             };
             for (int w = cluster_id; w < p.num_items && ok; w += num_clusters, ++items) {
                 const PairItem it = make_pair_item(w, p);
+                const int nb = it.nb[g];
                 auto slot_of = [&](int load) { return (kv_base + load) % kSlots; };
                 auto phase_of = [&](int load) { return static_cast<uint32_t>((kv_base + load) / kSlots) & 1u; };
-                ok = mbar_wait(q_full, static_cast<uint32_t>(items) & 1u, kFaultAttnWait, abort_flag) &&
-                     mbar_wait(kv_full(slot_of(0)), phase_of(0), kFaultAttnWait, abort_flag);
-                for (int g = 0; g < 2 && ok; ++g) {
-                    if (it.nb[g] == 0) continue;
-                    ok = s_writable(g);
-                    if (ok) {
-                        tc_fence_after();
-                        issue_s(g, kv_addr(slot_of(0)));
-                        ++s_issued[g];
-                    }
+                auto release_unused = [&](int load) {
+                    if (!mbar_wait(kv_full(slot_of(load)), phase_of(load), kFaultAttnWait, abort_flag)) return false;
+                    mma_commit_pair(kv_empty(slot_of(load)), 0x3);
+                    return true;
+                };
+                // Q of this item has landed: q_empty is in this item's phase.
+                ok = mbar_wait(q_full, static_cast<uint32_t>(items) & 1u, kFaultAttnWait, abort_flag);
+                if (ok && nb == 0) {
+                    for (int load = 0; load < 2 * it.nb_load && ok; ++load) ok = release_unused(load);
+                    if (ok) mma_commit_pair(q_empty, 0x3);
+                    kv_base += 2 * it.nb_load;
+                    continue;
                 }
+                ok = ok && mbar_wait(kv_full(slot_of(0)), phase_of(0), kFaultAttnWait, abort_flag) && s_writable();
                 if (!ok) break;
+                tc_fence_after();
+                issue_s(kv_addr(slot_of(0)));
+                ++s_issued;
                 mma_commit_pair(kv_empty(slot_of(0)), 0x3);
-                if (it.nb_load == 1) mma_commit_pair(q_empty, 0x3);
+                if (nb == 1) mma_commit_pair(q_empty, 0x3);
                 for (int j = 0; j < it.nb_load && ok; ++j) {
                     ok = false;
-                    // S of block j + 1 for both tiles: runs while the softmax of block j does.
-                    // Each tile's group is issued as soon as its own condition holds (waiting
-                    // for both tiles first measured slower: the pipe then idles on the later one).
+                    // S of block j + 1: runs while the softmax of block j does.
                     if (j + 1 < it.nb_load) {
                         const int k_load = 2 * (j + 1);
-                        if (!mbar_wait(kv_full(slot_of(k_load)), phase_of(k_load), kFaultAttnWait, abort_flag)) break;
-                        bool s_ok = true;
-                        for (int g = 0; g < 2 && s_ok; ++g) {
-                            if (j + 1 >= it.nb[g]) continue;
-                            s_ok = s_writable(g);
-                            if (s_ok) {
-                                tc_fence_after();
-                                issue_s(g, kv_addr(slot_of(k_load)));
-                                ++s_issued[g];
-                            }
+                        if (j + 1 < nb) {
+                            if (!mbar_wait(kv_full(slot_of(k_load)), phase_of(k_load), kFaultAttnWait, abort_flag) ||
+                                !s_writable())
+                                break;
+                            tc_fence_after();
+                            issue_s(kv_addr(slot_of(k_load)));
+                            ++s_issued;
+                            mma_commit_pair(kv_empty(slot_of(k_load)), 0x3);
+                            if (j + 1 == nb - 1) mma_commit_pair(q_empty, 0x3);
+                        } else if (!release_unused(k_load)) {
+                            break;
                         }
-                        if (!s_ok) break;
-                        mma_commit_pair(kv_empty(slot_of(k_load)), 0x3);
-                        if (j + 1 == it.nb_load - 1) mma_commit_pair(q_empty, 0x3);
                     }
-                    // PV of block j for both tiles, as each tile's P arrives.
+                    // PV of block j.
                     const int v_load = 2 * j + 1;
-                    if (!mbar_wait(kv_full(slot_of(v_load)), phase_of(v_load), kFaultAttnWait, abort_flag)) break;
-                    bool pv_ok = true;
-                    for (int g = 0; g < 2 && pv_ok; ++g) {
-                        if (j >= it.nb[g]) continue;
-                        pv_ok = mbar_wait(p_ready(g), static_cast<uint32_t>(pv_issued[g]) & 1u, kFaultAttnWait,
-                                          abort_flag);
+                    if (j < nb) {
+                        if (!mbar_wait(kv_full(slot_of(v_load)), phase_of(v_load), kFaultAttnWait, abort_flag) ||
+                            !mbar_wait(p_ready(g), static_cast<uint32_t>(pv_issued) & 1u, kFaultAttnWait, abort_flag))
+                            break;
                         // The first PV of an item overwrites O_g: the previous item's O_g must
                         // have been read out of tensor memory by both CTAs.
-                        if (pv_ok && j == 0 && outputs[g] > 0)
-                            pv_ok = mbar_wait(o_empty(g), static_cast<uint32_t>(outputs[g] - 1) & 1u, kFaultAttnWait,
-                                              abort_flag);
-                        if (pv_ok) {
-                            tc_fence_after();
-                            issue_pv(g, kv_addr(slot_of(v_load)), j == 0);
-                            ++pv_issued[g];
-                        }
+                        if (j == 0 && outputs > 0 &&
+                            !mbar_wait(o_empty(g), static_cast<uint32_t>(outputs - 1) & 1u, kFaultAttnWait, abort_flag))
+                            break;
+                        tc_fence_after();
+                        issue_pv(kv_addr(slot_of(v_load)), j == 0);
+                        ++pv_issued;
+                        mma_commit_pair(kv_empty(slot_of(v_load)), 0x3);
+                    } else if (!release_unused(v_load)) {
+                        break;
                     }
-                    if (!pv_ok) break;
-                    mma_commit_pair(kv_empty(slot_of(v_load)), 0x3);
                     ok = true;
                 }
-                for (int g = 0; g < 2; ++g)
-                    if (it.nb[g] > 0) ++outputs[g];
+                ++outputs;
                 kv_base += 2 * it.nb_load;
             }
         }
@@ -503,35 +509,46 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // V [bh_kv, S, 128] -> V^T [bh_kv, 128, s_pad] (binary16), keys S..s_pad-1 zero.
-// One 256-thread block per (64-key block, slice): 16-byte loads of 64 rows x 256 B
-// through a padded shared tile, 16-byte stores of 128 rows x 128 B.
+// One 256-thread block per (64-key block, slice). Loads: a warp reads two whole
+// 256-byte key rows (16-byte chunks, coalesced). Each thread packs the same head-dim
+// column of two keys into one 32-bit word, so the shared tile holds key pairs,
+// [128 head-dim rows][32 key pairs + 1]: the odd row pitch spreads a warp's
+// transposing stores over 8 banks per key pair (at most 4 lanes per bank) and makes
+// the reads of 4 consecutive key pairs conflict-free. Stores: 16-byte chunks of 8
+// keys, 8 lanes per 128-byte V^T row segment.
 __global__ void __launch_bounds__(256) transpose_v_kernel(const uint16_t* __restrict__ v, uint16_t* __restrict__ vt,
                                                           int seq, int s_pad, int slices) {
-    __shared__ uint16_t tile[128][64 + 8];
+    __shared__ uint32_t tile[128][33];
     const int k0 = static_cast<int>(blockIdx.x) * 64;
+    const int t = static_cast<int>(threadIdx.x);
     for (int slice = static_cast<int>(blockIdx.y); slice < slices; slice += static_cast<int>(gridDim.y)) {
         const uint16_t* src = v + static_cast<long long>(slice) * seq * 128LL;
         uint16_t* dst = vt + static_cast<long long>(slice) * 128LL * s_pad;
         __syncthreads();  // the previous slice's tile has been stored
-        for (int ci = static_cast<int>(threadIdx.x); ci < 64 * 16; ci += 256) {
-            const int key = ci >> 4;
-            const int d0 = (ci & 15) * 8;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (k0 + key < seq)
-                val = *reinterpret_cast<const uint4*>(src + static_cast<long long>(k0 + key) * 128 + d0);
-            const uint16_t* e = reinterpret_cast<const uint16_t*>(&val);
+        // 32 key pairs x 16 head-dim chunks of 8 = 512 units, two per thread.
+        for (int u = t; u < 512; u += 256) {
+            const int dc = u & 15;   // head-dim chunk: columns 8 dc .. 8 dc + 7
+            const int kp = u >> 4;   // key pair: keys k0 + 2 kp, k0 + 2 kp + 1
+            const int key = k0 + 2 * kp;
+            uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+            if (key < seq) lo = *reinterpret_cast<const uint4*>(src + static_cast<long long>(key) * 128 + 8 * dc);
+            if (key + 1 < seq) hi = *reinterpret_cast<const uint4*>(src + static_cast<long long>(key + 1) * 128 + 8 * dc);
+            const uint32_t a[4] = {lo.x, lo.y, lo.z, lo.w};
+            const uint32_t b[4] = {hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
-            for (int t = 0; t < 8; ++t) tile[d0 + t][key] = e[t];
+            for (int w = 0; w < 4; ++w) {
+                // columns 8 dc + 2 w (low halves) and 8 dc + 2 w + 1 (high halves)
+                tile[8 * dc + 2 * w][kp] = (a[w] & 0xffffu) | (b[w] << 16);
+                tile[8 * dc + 2 * w + 1][kp] = (a[w] >> 16) | (b[w] & 0xffff0000u);
+            }
         }
         __syncthreads();
-        for (int ci = static_cast<int>(threadIdx.x); ci < 128 * 8; ci += 256) {
-            const int d = ci >> 3;
-            const int kc = (ci & 7) * 8;
-            uint4 out;
-            uint16_t* e = reinterpret_cast<uint16_t*>(&out);
-#pragma unroll
-            for (int t = 0; t < 8; ++t) e[t] = tile[d][kc + t];
-            *reinterpret_cast<uint4*>(dst + static_cast<long long>(d) * s_pad + k0 + kc) = out;
+        // 128 head-dim rows x 8 chunks of 8 keys = 1024 units, four per thread.
+        for (int u = t; u < 1024; u += 256) {
+            const int d = u >> 3;
+            const int kc = u & 7;  // keys k0 + 8 kc .. k0 + 8 kc + 7 = key pairs 4 kc .. 4 kc + 3
+            const uint4 out = make_uint4(tile[d][4 * kc], tile[d][4 * kc + 1], tile[d][4 * kc + 2], tile[d][4 * kc + 3]);
+            *reinterpret_cast<uint4*>(dst + static_cast<long long>(d) * s_pad + k0 + 8 * kc) = out;
         }
     }
 }
