@@ -86,13 +86,23 @@ struct PairItem {
     int nb_load;  // key blocks loaded: max(nb[0], nb[1])
 };
 
-// Item w: (batch, head) w / quads, query rows [q0, q0 + 512) with the later (under
-// causal masking heavier) quads of a (batch, head) first; the items of one (batch,
-// head) are adjacent so that pairs running at one time share its K and V in L2.
+// Item w: a (batch, head) slice and query rows [q0, q0 + 512). The slices are taken
+// in groups of kItemGroup; inside a group the items run by quad, later (under causal
+// masking heavier) quads first, slice by slice. Pairs take items w = pair, pair + pairs,
+// ... (static), so the heavy and light quads spread over all pairs (simulated causal
+// imbalance, max over mean: 1.06, against 1.13 when the quads of a slice are adjacent),
+// while the pairs running at one time touch the K and V of about one group (32 MiB at
+// S = 4096), which stays in L2.
+constexpr int kItemGroup = 16;
+
 __device__ __forceinline__ PairItem make_pair_item(int w, const PairParams& p) {
     PairItem it;
-    it.bh = w / p.quads;
-    const int quad = p.quads - 1 - w % p.quads;
+    const int per_group = kItemGroup * p.quads;
+    const int g0 = (w / per_group) * kItemGroup;
+    const int gsize = min(kItemGroup, p.bh - g0);
+    const int within = w - (w / per_group) * per_group;
+    it.bh = g0 + within % gsize;
+    const int quad = p.quads - 1 - within / gsize;
     it.bh_kv = (it.bh / p.heads_q) * p.heads_kv + (it.bh % p.heads_q) / p.group;
     it.q0 = quad * kRowsPerItem;
     for (int g = 0; g < 2; ++g) {
