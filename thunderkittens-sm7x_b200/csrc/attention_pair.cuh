@@ -357,7 +357,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_bits = (quarter * 32u) << 16;
         const uint32_t s_addr = tmem + lane_bits + 128u * g;
         const uint32_t o_addr = tmem + lane_bits + 256u + 128u * g;
-        const uint32_t p_row = base + kPOff + g * kTileBytes + static_cast<uint32_t>(row) * 128u;
+        // This thread's P row in shared memory; plain stores (no asm), so the compiler can
+        // interleave them with the exponentials. fence.proxy.async orders them before the
+        // MMAs read P.
+        uint8_t* const p_row = smem + kPOff + g * kTileBytes + row * 128;
         const uint32_t swz = static_cast<uint32_t>(row & 7);
         const uint32_t s_free_lead = mapa_shared(s_free(g), 0);
         const uint32_t p_ready_lead = mapa_shared(p_ready(g), 0);
@@ -443,9 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         acc[i] = add2(acc[i], e);
                         pk[i] = pack_half2(e.x, e.y);
                     }
-                    const uint32_t addr = p_row + static_cast<uint32_t>(ch >> 3) * 16384u +
-                                          ((static_cast<uint32_t>(ch & 7) ^ swz) << 4);
-                    st_shared_v4(addr, pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4*>(p_row + (ch >> 3) * 16384 + ((static_cast<uint32_t>(ch & 7) ^ swz) << 4)) =
+                        make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
                 if (shared_block) {
                     __syncwarp();
