@@ -18,6 +18,7 @@ all-gather), and the hosts' copy bandwidth with every rank copying at once.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload headline|gemm|attention|rowops] [--gather [fused|nccl]]
                     [--no-configs] [--no-cpu-baseline]
+    python bench.py --sustained SECONDS   # power-capped rates, ours beside cuBLAS / cuDNN
 
 Timing: K steps between two CUDA events on the launching stream, a barrier and
 torch.cuda.synchronize() on both sides, the max over ranks. Headline inputs are
@@ -845,6 +846,82 @@ def run_multi_gpu(rank, world, peaks, iters=10):
     return out
 
 
+def run_sustained(seconds: float):
+    """Sustained rates under the 1 kW power cap, one GPU: each kernel back to back for
+    `seconds` (events around batches of 10 calls), with nvidia-smi sampling the SM clock
+    and board power meanwhile. Ours: the 8192^3 GEMM and the [8,32,4096,128] attention
+    (unmasked, causal). For comparison on the same GPU, library kernels of the same
+    shapes: cuBLAS FP16 x FP16 -> FP32 (torch.mm with out_dtype) and cuDNN's attention
+    (torch SDPA, binary16 output). Prints one JSON line."""
+    import torch
+    import torch.nn.functional as F
+    import tk_b200
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1)
+    rows = []
+
+    def measure(name, fn, flops, library=False):
+        try:
+            fn()
+            torch.cuda.synchronize()
+        except Exception as e:  # a library kernel this build of torch does not offer
+            rows.append({"kernel": name, "unavailable": str(e).splitlines()[0][:160]})
+            return
+        smi = subprocess.Popen(["nvidia-smi", "--query-gpu=clocks.sm,power.draw,clocks_event_reasons.active",
+                                "--format=csv,noheader,nounits", "-lms", "50", "-i",
+                                str(torch.cuda.current_device())], stdout=subprocess.PIPE, text=True)
+        time.sleep(0.3)
+        per_call = []
+        t0 = time.time()
+        while time.time() - t0 < seconds:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(10):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            per_call.append(e0.elapsed_time(e1) / 10)
+        smi.terminate()
+        samples = [r.split(",") for r in smi.communicate()[0].strip().splitlines() if r.count(",") == 2]
+        mhz = [float(s[0]) for s in samples]
+        watts = [float(s[1]) for s in samples]
+        ms = statistics.median(per_call)
+        rows.append({"kernel": name, "library": library, "calls": 10 * len(per_call),
+                     "first_batch_TFLOP/s": round(flops / per_call[0] / 1e9, 1),
+                     "sustained_TFLOP/s": round(flops / ms / 1e9, 1), "ms_per_call": round(ms, 4),
+                     "sm_mhz_median": statistics.median(mhz) if mhz else None,
+                     "power_w_median": statistics.median(watts) if watts else None,
+                     "reasons": sorted({s[2].strip() for s in samples})})
+
+    def check(code):
+        if code != 0:
+            raise RuntimeError(f"call failed with cudaError {code}")
+
+    n = GEMM_M
+    a = (torch.rand(n, n, device="cuda", generator=gen) * 2 - 1).half()
+    b = (torch.rand(n, n, device="cuda", generator=gen) * 2 - 1).half()
+    c = torch.empty(n, n, device="cuda")
+    measure("gemm_8192_fp16_fp32", lambda: check(tk_b200.gemm_raw(n, n, n, a, n, b, n, c, n)), gemm_flops())
+    measure("cublas_gemm_8192_fp16_fp32", lambda: torch.mm(a, b, out_dtype=torch.float32), gemm_flops(), True)
+    del a, b, c
+    q = torch.randn(ATT_B, ATT_H, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    k = torch.randn(ATT_B, ATT_H, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    v = torch.randn(ATT_B, ATT_H, ATT_S, ATT_D, device="cuda", generator=gen).half()
+    o = torch.empty(ATT_B, ATT_H, ATT_S, ATT_D, device="cuda")
+    scale = 1.0 / math.sqrt(ATT_D)
+    for causal in (False, True):
+        tag = "_causal" if causal else ""
+        measure("attention_fwd" + tag, lambda causal=causal: check(
+            tk_b200.attention_raw(q, k, v, o, ATT_B, ATT_H, ATT_S, ATT_D, scale, causal)), attn_flops(causal))
+
+        def cudnn(causal=causal):
+            from torch.nn.attention import SDPBackend, sdpa_kernel
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+        measure("cudnn_attention_fwd" + tag, cudnn, attn_flops(causal), True)
+    print(json.dumps({"sustained": rows, "seconds_per_kernel": seconds, "status": tk_b200.device_status()}))
+
+
 def workload_config(args, world):
     """The `config` object of both arms' JSON lines."""
     return {
@@ -1032,7 +1109,16 @@ def main():
                     help="head_dim 128 attention kernel: single-CTA (default) or CTA pair (tcgen05 cta_group::2)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the per-configuration (N = 1) and multi-GPU (N > 1) measurements")
+    ap.add_argument("--sustained", type=float, default=0.0, metavar="SECONDS",
+                    help="instead of the benchmark line: sustained rates under the power cap (one GPU), each "
+                         "kernel back to back for SECONDS, with cuBLAS / cuDNN kernels of the same shapes "
+                         "measured beside ours")
     args = ap.parse_args()
+    if args.sustained > 0:
+        if args.gpus != 1:
+            raise SystemExit("--sustained runs on one GPU")
+        run_sustained(args.sustained)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":
