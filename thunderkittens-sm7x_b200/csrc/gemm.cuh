@@ -100,6 +100,20 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
     *tn = r / rows;
 }
 
+// K-block of the i-th stage of a work unit: ascending for the CTA's even-numbered
+// units and descending for its odd ones when K is not split. All CTAs turn round
+// together, so a wave of tiles starts on the K-slices the previous wave read last,
+// which are still in L2 (consecutive waves of one rasterisation group share their
+// A rows). The order of the K-blocks changes the FP32 summation order of a tile,
+// which stays inside the GEMM's error bound; split-K units keep ascending order, so
+// both split reductions see identical partial sums.
+#ifndef TK_GEMM_SNAKE_K
+#define TK_GEMM_SNAKE_K 1
+#endif
+__device__ __forceinline__ int k_block_of(int i, int kb0, int kb1, int seq, const Params& p) {
+    return (TK_GEMM_SNAKE_K != 0 && p.k_splits == 1 && (seq & 1)) ? kb1 - 1 - i : kb0 + i;
+}
+
 // Output tile and K-block range of work unit t.
 __device__ __forceinline__ void work_coords(int t, const Params& p, int* tm, int* tn, int* kb0, int* kb1) {
     const int ks = t % p.k_splits;
@@ -205,12 +219,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         int issued = 0;
         bool ok = true;
         const uint32_t leader_full0 = kCtaGroup == 2 ? mapa_shared(full_bar(0), 0) : full_bar(0);
-        for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
+        for (int t = cluster_id, seq = 0; t < p.num_tiles && ok; t += num_clusters, ++seq) {
             int tm, tn, kb0, kb1;
             work_coords(t, p, &tm, &tn, &kb0, &kb1);
             const int row0 = tm * C::kTileM + static_cast<int>(rank) * kBlockM;
             const int col0 = tn * kBN + static_cast<int>(rank) * C::kBCols;
-            for (int kb = kb0; kb < kb1; ++kb) {
+            for (int i = 0; i < kb1 - kb0; ++i) {
+                const int kb = k_block_of(i, kb0, kb1, seq, p);
                 if (!mbar_wait_warp(empty_bar(stage), phase ^ 1u, kFaultProducerWait, abort_flag)) {
                     ok = false;
                     break;
@@ -269,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int tm, tn, kb0, kb1;
                 work_coords(t, p, &tm, &tn, &kb0, &kb1);
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-                for (int kb = kb0; kb < kb1; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {  // stages arrive in the producer's K order
                     if (!mbar_wait_warp(full_bar(stage), phase, kFaultMmaWait, abort_flag)) {
                         ok = false;
                         break;
