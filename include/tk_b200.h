@@ -234,8 +234,10 @@ TK_API int tk_gemm_set_small_m(int mode);
 
 /* No counterpart in the reference (a tuning switch). Tile-rows per rasterisation
  * group of the GEMM kernels' persistent tile walk: 0 (default) chooses by output shape
- * (16, or 32 when the output has at most 16 tile-columns); 1..4096 forces a value. Results
- * do not depend on it. Returns the previous setting; other values only query it.
+ * (16, or 32 when the output has at most 16 tile-columns); 1..4096 forces a value. The
+ * walk decides which tiles sum their K-blocks in descending order (every other tile of
+ * each CTA, when K is not split), so the last bits of C may change with it, inside the
+ * same error bound. Returns the previous setting; other values only query it.
  * Process-wide; every call reads it. */
 TK_API int tk_gemm_set_group_rows(int rows);
 
