@@ -468,20 +468,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) {
                 const uint32_t q_addr[2] = {base + C::kQOffset, base + C::kQOffset + C::kTileBytes};
                 auto kv_addr = [&](int slot) { return base + C::kKvOffset + slot * C::kTileBytes; };
+                // The start address sits in the low 14 bits of a descriptor (16-byte units)
+                // and every tile ends below 256 KiB, so a step inside a tile is a plain add
+                // to the tile's base descriptor. This thread's instruction stream sets the
+                // pace (a clock64 trace: ~75 cycles per MMA issued, the tensor pipe done
+                // ~150 cycles after the last one of a group), so it is kept short.
+                const uint64_t dq[2] = {sw128_desc(q_addr[0], 16, 1024), sw128_desc(q_addr[1], 16, 1024)};
                 auto issue_s = [&](int g, uint32_t k_addr) {
+                    const uint64_t dk = sw128_desc(k_addr, 16, 1024);
     #pragma unroll
                     for (int kk = 0; kk < kDPad / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-                        mma_f16_ss<1>(tmem + 256u * g, sw128_desc(q_addr[g] + off, 16, 1024),
-                                      sw128_desc(k_addr + off, 16, 1024), C::kIdescS, kk > 0 ? 1u : 0u);
+                        const uint64_t off = static_cast<uint64_t>(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+                        mma_f16_ss<1>(tmem + 256u * g, dq[g] + off, dk + off, C::kIdescS, kk > 0 ? 1u : 0u);
                     }
                     mma_commit(s_full(g));
                 };
                 auto issue_pv = [&](int g, uint32_t v_addr, bool first) {
+                    const uint64_t dv = sw128_desc(v_addr, 16384, 1024);
     #pragma unroll
                     for (int kk = 0; kk < kBlockKV / 16; ++kk)
                         mma_f16_ts(tmem + 256u * g + 128u, tmem + 256u * g + kk * 8,
-                                   sw128_desc(v_addr + kk * 2048, 16384, 1024), C::kIdescO,
+                                   dv + static_cast<uint64_t>((kk * 2048) >> 4), C::kIdescO,
                                    (!first || kk > 0) ? 1u : 0u);
                 };
                 uint32_t pr_phase[2] = {0, 0};
