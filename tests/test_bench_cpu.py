@@ -30,3 +30,12 @@ def test_reference_arm_other_ranks_exit_quietly():
     out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
                           "--warmup", "0"], capture_output=True, text=True, timeout=120, cwd=ROOT, env=env)
     assert out.returncode == 0 and out.stdout.strip() == ""
+
+
+def test_sustained_mode_is_single_gpu():
+    """The power-capped comparison mode runs on one GPU only and refuses other counts
+    before touching a device."""
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--sustained", "1", "--gpus", "2"],
+                         capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert out.returncode != 0
+    assert "one GPU" in out.stderr
